@@ -1,0 +1,309 @@
+"""Generate the golden fixtures in this folder by running the REFERENCE itself.
+
+Usage (needs a checkout of the reference Chenxing repo; it is pure NumPy):
+
+    python tests/golden/make_golden.py --reference <path-to-chenxing-checkout>
+
+Writes:
+  attention.npz   reference flash/naive attention outputs for the reference's
+                  own test shapes plus decode / verify / window / bf16 / dv!=d
+                  / explicit-mask cases; inputs are rebuilt from cases.py and
+                  pinned by the digests in attention_cases.json.
+  paged_cfg1.npz  the cfg1 decode run driven through the reference
+                  RadixPagedKVCache.write_layer -> read_layer -> flash_attention
+                  (chenxing/model/transformer.py:87-94), outputs at a few steps
+                  and a digest of the seeded inputs.
+  paged_bf16.npz  a cfg2-shaped bf16 (ml_dtypes) pool, one decode step
+                  (inputs from cases.paged_bf16_inputs, pinned by digest).
+  radix_ops.json  a seeded script of pool / radix-tree operations replayed on
+                  the reference with a logical LRU clock, with every result.
+  engine_meta.json block-table growth (LLMEngine._ensure_capacity), speculative
+                  rollback (SpeculativeDecoder._sync_to) and the slot each
+                  written token landed in, observed from the reference pool.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import itertools
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+
+
+def digest(*arrays) -> str:
+    h = hashlib.sha256()
+    for a in arrays:
+        a = np.ascontiguousarray(a)
+        h.update(str(a.dtype).encode())
+        h.update(str(a.shape).encode())
+        h.update(a.tobytes())
+    return h.hexdigest()
+
+
+def attention_outputs(ref_attn, CausalMask):
+    from cases import attention_cases, case_digest
+    out, meta = {}, []
+    for c in attention_cases():
+        if c["mask"] == "causal":
+            m = CausalMask(sliding_window=c["window"])
+        elif c["mask"] == "explicit":
+            m = c["explicit"]
+        else:
+            m = None
+        fn = ref_attn.flash_attention if c["use"] == "flash" else ref_attn.naive_attention
+        out[c["name"]] = fn(c["q"], c["k"], c["v"], m, c["scale"])
+        meta.append({"name": c["name"], "digest": case_digest(c)})
+    return out, meta
+
+
+def paged_cfg1(RadixPagedKVCache, flash, CausalMask):
+    from chenxing_b200.workloads import cfg1
+    wl, data = cfg1(seed=0)
+    cache = RadixPagedKVCache(wl.n_blocks, wl.block_size, 1, wl.n_kv_heads,
+                              wl.head_dim, dtype=np.float32)
+    ctx = wl.ctx_lens.copy()
+    for b in range(wl.batch):
+        cache.write_layer(wl.block_tables[b], 0, 0, data["k_pre"][b], data["v_pre"][b])
+    keep = [0, 1, 15, 31]
+    res = {}
+    for s in range(wl.steps):
+        outs = []
+        for b in range(wl.batch):
+            bt = wl.block_tables[b]
+            cache.write_layer(bt, int(ctx[b]), 0, data["k"][s, b][None], data["v"][s, b][None])
+            ka, va = cache.read_layer(bt, int(ctx[b]) + 1, 0)
+            q4 = data["q"][s, b][:, None, :][None]                       # (1, hq, 1, d)
+            k4 = np.ascontiguousarray(np.transpose(ka, (1, 0, 2))[None])
+            v4 = np.ascontiguousarray(np.transpose(va, (1, 0, 2))[None])
+            outs.append(flash(q4, k4, v4, CausalMask())[0][:, 0, :])     # (hq, d)
+            ctx[b] += 1
+        if s in keep:
+            res[f"out_step{s}"] = np.stack(outs)
+    res["final_ctx"] = ctx
+    res["input_digest"] = np.frombuffer(
+        digest(wl.ctx_lens, np.asarray(sum(wl.block_tables, [])),
+               *data["k_pre"], *data["v_pre"], data["q"], data["k"], data["v"]).encode(),
+        dtype=np.uint8)
+    res["pool_digest"] = np.frombuffer(digest(cache.k_pool, cache.v_pool).encode(),
+                                       dtype=np.uint8)
+    return res
+
+
+def paged_bf16(RadixPagedKVCache, flash, CausalMask, bf16):
+    from cases import paged_bf16_inputs
+    wl, ks, vs, qs = paged_bf16_inputs()
+    cache = RadixPagedKVCache(wl.n_blocks, wl.block_size, 1, wl.n_kv_heads,
+                              wl.head_dim, dtype=bf16)
+    outs, bits = [], []
+    for b in range(wl.batch):
+        c = int(wl.ctx_lens[b]) + 1
+        cache.write_layer(wl.block_tables[b], 0, 0, ks[b], vs[b])
+        ka, va = cache.read_layer(wl.block_tables[b], c, 0)
+        q4 = qs[b][:, None, :][None]
+        k4 = np.ascontiguousarray(np.transpose(ka, (1, 0, 2))[None])
+        v4 = np.ascontiguousarray(np.transpose(va, (1, 0, 2))[None])
+        outs.append(flash(q4, k4, v4, CausalMask())[0][:, 0, :])
+        bits.append(ka.view(np.uint16))
+    return {"out": np.stack(outs),
+            "input_digest": np.frombuffer(digest(*ks, *vs, *qs).encode(), dtype=np.uint8),
+            "kbits_digest": np.frombuffer(digest(*bits).encode(), dtype=np.uint8)}
+
+
+def radix_script(ref_radix, n_ops=700, seed=5):
+    """Seeded request-driven workload over the reference cache.
+
+    Requests draw prompts from a few shared documents so prefixes hit; each
+    op and its result (block ids, hit lengths, node handles, freed counts,
+    error class, FIFO free-list order, stats) is recorded for replay.
+    """
+    clock = itertools.count()
+    ref_radix.time.monotonic = lambda: float(next(clock))
+    bs = 4
+    cache = ref_radix.RadixPagedKVCache(n_blocks=40, block_size=bs, n_layers=1,
+                                        n_kv_heads=1, head_dim=2)
+    rng = np.random.default_rng(seed)
+    docs = [[int(t) for t in rng.integers(0, 6, 28)] for _ in range(5)]
+    handles = [None]          # handle 0 = "no node"
+    pinned = []
+    ops = []
+    last_hit = {"blocks": [], "node": 0, "tokens": []}
+
+    def h_of(node):
+        for i, n in enumerate(handles):
+            if n is node:
+                return i
+        handles.append(node)
+        return len(handles) - 1
+
+    def snapshot():
+        return {"free": list(cache._free.keys()), "stats": cache.stats()}
+
+    for _ in range(n_ops):
+        r = rng.random()
+        rec = {}
+        try:
+            if r < 0.25:
+                d = docs[int(rng.integers(0, len(docs)))]
+                n = int(rng.integers(1, len(d) + 1))
+                toks = d[:n] + [int(t) for t in rng.integers(0, 6, int(rng.integers(0, 5)))]
+                rec = {"op": "match", "tokens": toks}
+                hit = cache.match_prefix(toks)
+                rec["res"] = {"n_tokens": hit.n_tokens, "blocks": list(hit.block_ids),
+                              "node": h_of(hit.node)}
+                last_hit = {"blocks": list(hit.block_ids), "node": rec["res"]["node"],
+                            "tokens": toks}
+            elif r < 0.45:
+                # publish a block-aligned chain: either the last hit's request
+                # (prefix blocks reused, rest freshly allocated) or a new doc slice
+                if last_hit["tokens"] and rng.random() < 0.6:
+                    toks = last_hit["tokens"]
+                    prefix_blocks = list(last_hit["blocks"])
+                    parent = last_hit["node"] if rng.random() < 0.4 else None
+                else:
+                    d = docs[int(rng.integers(0, len(docs)))]
+                    toks = d[:int(rng.integers(1, len(d) + 1))]
+                    prefix_blocks, parent = [], None
+                n_al = (len(toks) // bs) * bs
+                toks = toks[:n_al]
+                nb = n_al // bs - len(prefix_blocks)
+                if parent is not None:
+                    prefix_blocks = []
+                    nb = n_al // bs
+                if nb < 0 or n_al == 0:
+                    continue
+                rec = {"op": "insert", "tokens": toks, "nb": nb,
+                       "prefix_blocks": prefix_blocks, "parent": parent}
+                got = []
+                try:
+                    for _ in range(nb):
+                        got.append(cache.alloc_block())
+                except ref_radix.OutOfKVCacheError:
+                    for b in got:
+                        cache._free_block(b)
+                    rec["alloc"] = got
+                    raise
+                rec["alloc"] = got
+                node = cache.insert(toks, prefix_blocks + got,
+                                    parent=handles[parent] if parent else None)
+                rec["res"] = h_of(node)
+            elif r < 0.57 and len(handles) > 1:
+                hd = int(rng.integers(1, len(handles)))
+                rec = {"op": "acquire", "node": hd}
+                cache.acquire(handles[hd])
+                pinned.append(hd)
+            elif r < 0.70 and len(handles) > 1:
+                if pinned and rng.random() < 0.9:
+                    hd = pinned.pop(int(rng.integers(0, len(pinned))))
+                else:
+                    hd = int(rng.integers(1, len(handles)))
+                rec = {"op": "release", "node": hd}
+                cache.release(handles[hd])
+            elif r < 0.80:
+                rec = {"op": "evict", "n": int(rng.integers(1, 6))}
+                rec["res"] = cache.evict(rec["n"])
+            elif r < 0.88:
+                rec = {"op": "ensure_free", "n": int(rng.integers(1, 16))}
+                cache.ensure_free(rec["n"])
+            elif r < 0.93:
+                rec = {"op": "alloc"}
+                rec["res"] = cache.alloc_block()
+            else:
+                rec = {"op": "free", "bid": int(rng.integers(0, 40))}
+                cache._free_block(rec["bid"])
+        except Exception as e:      # noqa: BLE001 - the error class is the result
+            rec["error"] = type(e).__name__
+        if rec:
+            ops.append({**rec, "after": snapshot()})
+    return {"n_blocks": 40, "block_size": bs, "ops": ops,
+            "final_tree": tree_sig(cache._root)}
+
+
+def tree_sig(n):
+    return [list(n.tokens), list(n.blocks), n.refcnt,
+            [[k, tree_sig(c)] for k, c in n.children.items()]]
+
+
+def engine_meta(ref_radix, LLMEngine, seed=9):
+    """Block-table growth + speculative rollback as the reference engine does it."""
+    clock = itertools.count()
+    ref_radix.time.monotonic = lambda: float(next(clock))
+    bs = 16
+    cache = ref_radix.RadixPagedKVCache(n_blocks=256, block_size=bs, n_layers=1,
+                                        n_kv_heads=1, head_dim=1)
+
+    class Stub:                      # the engine state _ensure_capacity touches
+        kv = cache
+
+        def _preempt_oldest(self):
+            raise ref_radix.OutOfKVCacheError("preempt not modelled in fixture")
+
+    class Seq:
+        def __init__(self):
+            self.block_table = []
+            self.n_tokens = 0
+
+    rng = np.random.default_rng(seed)
+    seqs = [Seq() for _ in range(6)]
+    trace = []
+    for step in range(40):
+        i = int(rng.integers(0, len(seqs)))
+        s = seqs[i]
+        gamma = int(rng.choice([1, 4, 8]))
+        t = gamma + 1
+        LLMEngine._ensure_capacity(Stub(), s, s.n_tokens + t)
+        # observe where each written token lands, via unique markers
+        marks = (np.arange(t, dtype=np.float32) + 1000.0 * (step + 1)).reshape(t, 1, 1)
+        cache.write_layer(s.block_table, s.n_tokens, 0, marks, marks)
+        flat = cache.k_pool[0, :, :, 0, 0].reshape(-1)
+        slots = [int(np.flatnonzero(flat == m)[0]) for m in marks.reshape(-1)]
+        start = s.n_tokens
+        s.n_tokens += t
+        rejected = int(rng.integers(0, gamma + 1))
+        target = s.n_tokens - rejected
+        if s.n_tokens > target:          # speculative.py:88-89
+            s.n_tokens = target
+        trace.append({"seq": i, "start": start, "t": t, "rejected": rejected,
+                      "slots": slots, "table": list(s.block_table),
+                      "n_tokens": s.n_tokens, "free": list(cache._free.keys())})
+    return {"block_size": bs, "n_blocks": 256, "n_seqs": len(seqs), "trace": trace}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path to a Chenxing checkout")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    sys.path.insert(0, ROOT)
+    import ml_dtypes
+    from chenxing.core import attention as ref_attn
+    from chenxing.core.tensor import CausalMask
+    from chenxing.engine import radix_kv as ref_radix
+    from chenxing.engine.engine import LLMEngine
+
+    bf16 = ml_dtypes.bfloat16
+    sys.path.insert(0, HERE)
+    arrs, cases = attention_outputs(ref_attn, CausalMask)
+    np.savez_compressed(os.path.join(HERE, "attention.npz"), **arrs)
+    with open(os.path.join(HERE, "attention_cases.json"), "w") as f:
+        json.dump(cases, f, indent=1)
+    np.savez_compressed(os.path.join(HERE, "paged_cfg1.npz"),
+                        **paged_cfg1(ref_radix.RadixPagedKVCache, ref_attn.flash_attention,
+                                     CausalMask))
+    np.savez_compressed(os.path.join(HERE, "paged_bf16.npz"),
+                        **paged_bf16(ref_radix.RadixPagedKVCache, ref_attn.flash_attention,
+                                     CausalMask, bf16))
+    with open(os.path.join(HERE, "radix_ops.json"), "w") as f:
+        json.dump(radix_script(ref_radix), f)
+    with open(os.path.join(HERE, "engine_meta.json"), "w") as f:
+        json.dump(engine_meta(ref_radix, LLMEngine), f)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()
