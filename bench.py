@@ -1,0 +1,550 @@
+"""Benchmark of the Chenxing KV hot path on B200: paged decode + KV append.
+
+Workload (cfg2, per GPU): Llama-3-8B-shaped decode, 64 sequences with
+contexts ~ U[1024, 8192], 32 layers, 32 query heads / 8 KV heads, head_dim
+128, bf16 KV pool with 16-token blocks scattered over a pool sized to 90 % of
+free HBM.  One step = for every layer: append one K/V token per sequence
+(cx_kv_append) then paged flash-decode over the full context
+(cx_paged_decode) — the reference's transformer.py:87-94 minus projections.
+Multi-GPU: one process per GPU, each with its own pool and 64 sequences
+(weak scaling), plus an NCCL all-gather of the step's attention rows.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Metric: KV token-layers per second (one cached position x one layer, all KV
+heads, K and V) and the HBM GB/s they imply; prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "paged-decode KV tokens/s (KV token-layers/s, cfg2 Llama-3-8B-shaped decode)"
+UNIT = "KV-token-layers/s"
+HQ, HK, D, BS, LAYERS, BATCH = 32, 8, 128, 16, 32, 64
+ELEM = 2  # bf16
+UNIT_BYTES = 2 * HK * D * ELEM  # K + V bytes per KV token-layer
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["cfg2", "small"], default="cfg2",
+                    help="small: 1 layer, pool sized to need (~2 GB, for profiler captures)")
+    ap.add_argument("--pool-frac", type=float, default=0.9)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+def workload_config(args, n_gpus, n_blocks, layers):
+    return {"workload": "cfg2: Llama-3-8B-shaped paged decode + KV append",
+            "model": "Llama-3-8B attention shape (synthetic, no weights)",
+            "global_batch": BATCH * n_gpus, "batch_per_gpu": BATCH,
+            "seq_len": "ctx ~ U[1024, 8192] (+1 per step)", "layers": layers,
+            "q_heads": HQ, "kv_heads": HK, "head_dim": D, "block_size": BS,
+            "kv_dtype": "bf16", "q_dtype": "bf16", "out_dtype": "fp32",
+            "pool_blocks_per_gpu": n_blocks,
+            "pool": "90% of free HBM, blocks scattered by permutation" if args.config == "cfg2"
+            else "sized to need",
+            "parallelism": f"sequence-sharded x{n_gpus} (own pool per GPU)",
+            "l2": "no flush: every layer reads ~600 MB of KV, > 126 MB L2"}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled with nvidia-smi during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 9]
+        if self.uuid:
+            mine = [r for r in rows if self.uuid in r[0]]
+            rows = mine or rows
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def device_uuid(dev):
+    import torch
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per KV token-layer of the decode kernel, from a committed
+    ncu summary (profiles/paged_attn_mma_cfg2.json), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "paged_attn_mma_cfg2.json")) as f:
+            return float(json.load(f)["dram_bytes_per_kv_token_layer"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's per-sequence path restated by the oracle
+# ---------------------------------------------------------------------------
+def _cpu_worker_init(seed, ctxs, idx):
+    global _W
+    import ml_dtypes
+    from oracle.radix_kv import OraclePagedKVCache
+    rng = np.random.default_rng(seed + 1000 * (idx[0] if idx else 0))
+    need = sum(-(-(int(c) + 64) // BS) for c in ctxs)
+    cache = OraclePagedKVCache(need, BS, 1, HK, D, dtype=ml_dtypes.bfloat16)
+    tables, o = [], 0
+    for c in ctxs:
+        n = -(-(int(c) + 64) // BS)
+        tables.append(list(range(o, o + n)))
+        o += n
+    for c, t in zip(ctxs, tables):
+        kv = (rng.standard_normal((int(c), HK, D)) / math.sqrt(D)).astype(np.float32)
+        cache.write_layer(t, 0, 0, kv, kv)
+    _W = {"cache": cache, "tables": tables, "ctx": [int(c) for c in ctxs], "rng": rng}
+
+
+def _cpu_worker_step(_):
+    from oracle.paged import attend_sequence
+    w = _W
+    n = 0
+    for i, t in enumerate(w["tables"]):
+        q = (w["rng"].standard_normal((1, HQ, D)) / math.sqrt(D)).astype(np.float32)
+        kn = (w["rng"].standard_normal((1, HK, D)) / math.sqrt(D)).astype(np.float32)
+        if w["ctx"][i] + 1 > len(t) * BS:
+            w["ctx"][i] -= 32          # stay inside the table on long runs
+        attend_sequence(w["cache"], t, w["ctx"][i], 0, q, kn, kn)
+        w["ctx"][i] += 1
+        n += w["ctx"][i]
+    return n
+
+
+def cpu_port_rate(ctx, seconds, procs, seed):
+    """KV token-layers/s of the oracle port (write_layer -> read_layer ->
+    flash_attention per sequence, one layer) over ``ctx``; returns
+    (rate, cores, description, steps_done)."""
+    import multiprocessing as mp
+    if procs <= 1:
+        _cpu_worker_init(seed, list(ctx), [0])
+        t0 = time.perf_counter()
+        units = 0
+        steps = 0
+        while True:
+            units += _cpu_worker_step(0)
+            steps += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        return units / (time.perf_counter() - t0), 1, steps
+    groups = [list(range(i, len(ctx), procs)) for i in range(procs)]
+    groups = [g for g in groups if g]
+    ctxm = mp.get_context("spawn")
+    pools = [ctxm.Pool(1, _cpu_worker_init, (seed, [ctx[i] for i in g], g)) for g in groups]
+    try:
+        for p in pools:                       # warm (includes pool build)
+            p.apply(_cpu_worker_step, (0,))
+        t0 = time.perf_counter()
+        units, steps = 0, 0
+        while True:
+            res = [p.apply_async(_cpu_worker_step, (0,)) for p in pools]
+            units += sum(r.get() for r in res)
+            steps += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        return units / (time.perf_counter() - t0), len(pools), steps
+    finally:
+        for p in pools:
+            p.terminate()
+
+
+def cpu_count():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference path's CPU restatement on all host cores
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from chenxing_b200.workloads import cfg2_meta
+    wl = cfg2_meta(n_blocks=BATCH * 600, seed=args.seed)
+    procs = max(1, min(cpu_count(), BATCH))
+    # step = one layer of the 64 sequences (bounded sample of the cfg2 step)
+    import multiprocessing as mp
+    groups = [list(range(i, BATCH, procs)) for i in range(procs)]
+    ctxm = mp.get_context("spawn")
+    pools = [ctxm.Pool(1, _cpu_worker_init, (args.seed, [int(wl.ctx_lens[i]) for i in g], g))
+             for g in groups if g]
+    try:
+        def step():
+            res = [p.apply_async(_cpu_worker_step, (0,)) for p in pools]
+            return sum(r.get() for r in res)
+        for _ in range(args.warmup):
+            step()
+        t0 = time.perf_counter()
+        units = sum(step() for _ in range(args.steps))
+        dt = time.perf_counter() - t0
+    finally:
+        for p in pools:
+            p.terminate()
+    rate = units / dt
+    sample = (f"1 of {LAYERS} layers x {BATCH} sequences per step (write_layer -> read_layer "
+              f"-> flash_attention per sequence, bf16 ml_dtypes pool)")
+    line = {"metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "impl": "reference",
+            "config": workload_config(args, args.gpus, 0, LAYERS),
+            "cpu_baseline": {"value": rate, "unit": UNIT, "cores": len(pools), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "reference is pure NumPy (no GPU path); timed as its CPU restatement "
+                    "in oracle/ on this host's cores"}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from chenxing_b200 import PagedBatch, RadixPagedKVCache, _lib
+    from chenxing_b200.batch import slot_mapping
+    from chenxing_b200.workloads import cfg2_meta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    layers = LAYERS if args.config == "cfg2" else 1
+    steps_total = args.warmup + args.steps
+    per_block = layers * 2 * BS * HK * D * ELEM
+    if args.config == "cfg2":
+        free, _ = torch.cuda.mem_get_info(dev)
+        n_blocks = int(args.pool_frac * free // per_block)
+    else:
+        n_blocks = BATCH * (-(-(8192 + steps_total) // BS)) + 64
+    wl = cfg2_meta(n_blocks=n_blocks, seed=args.seed + rank, batch=BATCH, steps=steps_total,
+                   n_layers=layers)
+    cache = RadixPagedKVCache(n_blocks, BS, layers, HK, D, dtype="bfloat16", device=dev,
+                              host_io=False)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    for t in (cache._k, cache._v):           # K, V ~ N(0,1)/sqrt(128), layer slab at a time
+        for l in range(layers):
+            t[l].normal_(0.0, 1.0 / math.sqrt(D), generator=g)
+
+    ctx0 = wl.ctx_lens.astype(np.int64)
+    n_sets = min(steps_total, 4)               # distinct per-step input sets, cycled
+    sc = 1.0 / math.sqrt(D)
+    q_in = (torch.randn((n_sets, layers, BATCH, HQ, D), device=dev, generator=g) * sc).bfloat16()
+    k_in = (torch.randn((n_sets, layers, BATCH, HK, D), device=dev, generator=g) * sc).bfloat16()
+    v_in = (torch.randn((n_sets, layers, BATCH, HK, D), device=dev, generator=g) * sc).bfloat16()
+    outs = torch.empty((layers, BATCH, HQ, D), dtype=torch.float32, device=dev)
+    batches, slots = [], []
+    for s in range(steps_total):
+        slots.append(torch.from_numpy(slot_mapping(wl.block_tables, ctx0 + s, [1] * BATCH, BS))
+                     .to(dev))
+        batches.append(PagedBatch(cache, wl.block_tables, ctx0 + s + 1, n_q_heads=HQ,
+                                  table_stride=max(len(t) for t in wl.block_tables)))
+    units_step = [int((ctx0 + s + 1).sum()) * layers for s in range(steps_total)]
+    gathered = torch.empty((world * BATCH, HQ, D), dtype=torch.float32, device=dev) \
+        if world > 1 else None
+
+    lib = _lib.lib()
+    pool = cache.cx_pool()
+    stream = torch.cuda.Stream(dev)
+    sp = stream.cuda_stream
+    launches = [0]
+
+    def one_step(s, ev=None):
+        bt = batches[s]
+        c = bt.c_struct()
+        ws, wsn = bt.workspace.data_ptr(), bt.workspace.numel()
+        x = s % n_sets
+        for l in range(layers):
+            _lib.check(lib.cx_kv_append(pool, l, k_in[x, l].data_ptr(), v_in[x, l].data_ptr(),
+                                        _lib.CX_BF16, slots[s].data_ptr(), BATCH, None, None,
+                                        None, 0, sp), "cx_kv_append")
+            if ev is not None:
+                ev[l][0].record(stream)
+            _lib.check(lib.cx_paged_decode(pool, l, c, q_in[x, l].data_ptr(), _lib.CX_BF16,
+                                           outs[l].data_ptr(), ws, wsn, int(l == 0), sp),
+                       "cx_paged_decode")
+            if ev is not None:
+                ev[l][1].record(stream)
+            launches[0] += 2 + (l == 0)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, outs[layers - 1])
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            one_step(s)
+        torch.cuda.synchronize(dev)
+        flags = _lib.device_flags(clear=True, device=dev)
+        if flags:
+            raise RuntimeError(f"device flags after warm-up: {_lib.describe_flags(flags)}")
+        sampler = ClockSampler(device_uuid(dev)) if rank == 0 else None
+        if sampler:
+            sampler.start()
+            time.sleep(0.5)
+        evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(layers)]
+               for _ in range(args.steps)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches[0] = 0
+        barrier()
+        torch.cuda.synchronize(dev)
+        start.record(stream)
+        for i in range(args.steps):
+            one_step(args.warmup + i, evs[i])
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        clocks = sampler.stop() if sampler else None
+        timed_launches = launches[0]
+    ms = start.elapsed_time(end)
+    dec_ms = [e[0].elapsed_time(e[1]) for step in evs for e in step]
+    flags = _lib.device_flags(clear=True, device=dev)
+    if flags:
+        raise RuntimeError(f"device flags during timing: {_lib.describe_flags(flags)}")
+
+    units = sum(units_step[args.warmup:])
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    u = torch.tensor([units], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(u, op=dist.ReduceOp.SUM)
+    ms_max, units_all = float(t.item()), float(u.item())
+    value = units_all / (ms_max / 1e3)
+
+    # roofline of the dominant kernel (paged decode), per launch
+    avg_dec_ms = float(np.mean(dec_ms))
+    kv_tok_layer = units / (args.steps * layers)        # keys per decode launch
+    nblk = sum(-(-int(c) // BS) for c in ctx0) + BATCH * (args.warmup + args.steps / 2) / BS
+    alg_bytes = kv_tok_layer * UNIT_BYTES + BATCH * HQ * D * (ELEM + 4) + 4 * nblk
+    achieved = alg_bytes / (avg_dec_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak()
+    tpu = profile_traffic()
+    roofline = {"bound": "hbm", "kernel": "paged_attn_mma_kernel", "achieved": achieved,
+                "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                "traffic": (tpu * kv_tok_layer) if tpu else None,
+                "algorithmic_bytes_per_launch": alg_bytes, "avg_launch_ms": avg_dec_ms,
+                "decode_share_of_step": sum(dec_ms) / ms}
+    step_gbs = (units * UNIT_BYTES) / (ms / 1e3) / 1e9
+
+    # end to end: inputs from pinned host memory and outputs back, every step
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, lib, pool, cache, batches, slots, layers, n_sets, dev, world,
+                      units_step, launches)
+        if world > 1:
+            te = torch.tensor([e2e.pop("_ms")], dtype=torch.float64, device=dev)
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+            e2e["value"] = units_all / (float(te.item()) / 1e3)
+        else:
+            e2e["value"] = units / (e2e.pop("_ms") / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, cores, steps_done = cpu_port_rate([int(c) for c in ctx0[:4]], args.cpu_seconds,
+                                                1, args.seed)
+        cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"4 cfg2 sequences (ctx {', '.join(str(int(c)) for c in ctx0[:4])}), "
+                         f"1 layer, {steps_done} decode steps of write_layer -> read_layer -> "
+                         f"flash_attention (oracle restatement, NumPy, bf16 pool)"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded N(0,1)/sqrt(128) K/V/Q)",
+                "config": workload_config(args, world, n_blocks, layers),
+                "hbm_gbs_step": step_gbs, "hbm_frac_step": step_gbs / peak,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": timed_launches, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def run_e2e(args, lib, pool, cache, batches, slots, layers, n_sets, dev, world, units_step,
+            launches):
+    """Same step through the C ABI, with every step's q / k_new / v_new taken
+    from pinned host memory (H2D inside the timed region, per layer on a copy
+    stream, overlapped with the previous layer's kernels) and every layer's
+    attention rows copied back to pinned host memory (D2H)."""
+    import torch
+    import torch.distributed as dist
+    from chenxing_b200 import _lib
+
+    sc = 1.0 / math.sqrt(D)
+    g = torch.Generator()
+    g.manual_seed(99)
+    hq = (torch.randn((n_sets, layers, BATCH, HQ, D), generator=g) * sc).bfloat16().pin_memory()
+    hk = (torch.randn((n_sets, layers, BATCH, HK, D), generator=g) * sc).bfloat16().pin_memory()
+    hv = (torch.randn((n_sets, layers, BATCH, HK, D), generator=g) * sc).bfloat16().pin_memory()
+    hout = torch.empty((layers, BATCH, HQ, D), dtype=torch.float32).pin_memory()
+    dq = torch.empty((2, BATCH, HQ, D), dtype=torch.bfloat16, device=dev)
+    dk = torch.empty((2, BATCH, HK, D), dtype=torch.bfloat16, device=dev)
+    dv = torch.empty((2, BATCH, HK, D), dtype=torch.bfloat16, device=dev)
+    dout = torch.empty((2, BATCH, HQ, D), dtype=torch.float32, device=dev)
+    main = torch.cuda.Stream(dev)
+    copy_in = torch.cuda.Stream(dev)
+    copy_out = torch.cuda.Stream(dev)
+    sp = main.cuda_stream
+    gathered = torch.empty((world * BATCH, HQ, D), dtype=torch.float32, device=dev) \
+        if world > 1 else None
+    # per-step scheduler metadata also comes from the host: context lengths
+    # (for the plan) and the append slots
+    hctx = [b.ctx_lens.cpu().pin_memory() for b in batches]
+    hslot = [t.cpu().pin_memory() for t in slots]
+    h2d = (hq[0, 0].numel() + hk[0, 0].numel() + hv[0, 0].numel()) * 2 * layers \
+        + hctx[0].numel() * 4 + hslot[0].numel() * 8
+    d2h = hout.numel() * 4
+
+    def step(s):
+        bt = batches[s]
+        c = bt.c_struct()
+        ws, wsn = bt.workspace.data_ptr(), bt.workspace.numel()
+        x = s % n_sets
+        in_ev = [torch.cuda.Event() for _ in range(layers)]
+        done_ev = [torch.cuda.Event() for _ in range(layers)]
+        out_ev = [torch.cuda.Event() for _ in range(layers)]
+        with torch.cuda.stream(copy_in):
+            bt.ctx_lens.copy_(hctx[s], non_blocking=True)
+            slots[s].copy_(hslot[s], non_blocking=True)
+        for l in range(layers):
+            j = l & 1
+            with torch.cuda.stream(copy_in):
+                if l >= 2:
+                    copy_in.wait_event(done_ev[l - 2])      # buffer j free again
+                dq[j].copy_(hq[x, l], non_blocking=True)
+                dk[j].copy_(hk[x, l], non_blocking=True)
+                dv[j].copy_(hv[x, l], non_blocking=True)
+                in_ev[l].record(copy_in)
+            main.wait_event(in_ev[l])
+            if l >= 2:
+                main.wait_event(out_ev[l - 2])            # dout[j] drained
+            _lib.check(lib.cx_kv_append(pool, l, dk[j].data_ptr(), dv[j].data_ptr(),
+                                        _lib.CX_BF16, slots[s].data_ptr(), BATCH, None, None,
+                                        None, 0, sp), "cx_kv_append")
+            _lib.check(lib.cx_paged_decode(pool, l, c, dq[j].data_ptr(), _lib.CX_BF16,
+                                           dout[j].data_ptr(), ws, wsn, int(l == 0), sp),
+                       "cx_paged_decode")
+            launches[0] += 2 + (l == 0)
+            done_ev[l].record(main)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(done_ev[l])
+                hout[l].copy_(dout[j], non_blocking=True)
+                out_ev[l].record(copy_out)
+        if world > 1:
+            with torch.cuda.stream(main):
+                dist.all_gather_into_tensor(gathered, dout[(layers - 1) & 1])
+        main.wait_stream(copy_out)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(main)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    end.record(main)
+    torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end)
+    return {"_ms": ms, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": ms / args.steps,
+            "path": "C ABI (cx_kv_append + cx_paged_decode), pinned host buffers, copies on "
+                    "side streams overlapped per layer"}
+
+
+def main():
+    args = parse()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

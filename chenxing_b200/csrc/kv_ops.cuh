@@ -1,0 +1,242 @@
+// KV pool data movement: slot-mapped append (+ copy-on-write of shared tail
+// blocks), the read_layer gather, and whole/partial block copies.
+// Pool layout: [n_layers][n_blocks][n_kv_heads][block_size][head_dim].
+#include "cx_common.cuh"  // unity build: included from cxkv.cu
+
+namespace cx {
+
+struct PoolGeom {
+    int64_t n_layers, n_blocks, block_size, n_kv_heads, head_dim;
+    // element offset of (layer, block, head, slot 0, dim 0)
+    __host__ __device__ __forceinline__ int64_t tile(int64_t layer, int64_t block,
+                                                     int64_t head) const {
+        return (((layer * n_blocks + block) * n_kv_heads + head) * block_size) * head_dim;
+    }
+};
+
+inline PoolGeom geom_of(const cx_pool* p) {
+    return PoolGeom{p->n_layers, p->n_blocks, p->block_size, p->n_kv_heads, p->head_dim};
+}
+
+// Cooperative byte copy over `n` threads (thread index `i`), widest vector
+// the alignment of both pointers and the length allow.
+__device__ __forceinline__ void copy_bytes(char* dst, const char* src, int64_t nbytes, int i,
+                                          int n) {
+    uintptr_t a = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) |
+                  static_cast<uintptr_t>(nbytes);
+    if ((a & 15) == 0) {
+        const uint4* s = reinterpret_cast<const uint4*>(src);
+        uint4* d = reinterpret_cast<uint4*>(dst);
+        for (int64_t k = i; k < nbytes / 16; k += n) d[k] = s[k];
+    } else if ((a & 3) == 0) {
+        const uint32_t* s = reinterpret_cast<const uint32_t*>(src);
+        uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+        for (int64_t k = i; k < nbytes / 4; k += n) d[k] = s[k];
+    } else {
+        const uint16_t* s = reinterpret_cast<const uint16_t*>(src);
+        uint16_t* d = reinterpret_cast<uint16_t*>(dst);
+        for (int64_t k = i; k < nbytes / 2; k += n) d[k] = s[k];
+    }
+}
+
+// One warp per job.  Jobs [0, n_tok*H) store token rows; jobs
+// [n_tok*H, (n_tok+n_cow)*H) copy the valid prefix of a shared tail block.
+template <typename S, typename P>
+__global__ void __launch_bounds__(256) kv_append_kernel(
+    P* __restrict__ kp, P* __restrict__ vp, PoolGeom g, int64_t layer,
+    const S* __restrict__ kn, const S* __restrict__ vn, const int64_t* __restrict__ slots,
+    int64_t n_tok, const int32_t* __restrict__ cow_src, const int32_t* __restrict__ cow_dst,
+    const int32_t* __restrict__ cow_nv, int64_t n_cow) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t H = g.n_kv_heads, D = g.head_dim;
+    const int64_t n_jobs = (n_tok + n_cow) * H;
+    for (int64_t job = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); job < n_jobs;
+         job += warps) {
+        const int64_t h = job % H;
+        const int64_t t = job / H;
+        if (t < n_tok) {
+            const int64_t slot = slots[t];
+            if (slot < 0) continue;  // padding token
+            if (slot >= g.n_blocks * g.block_size) {
+                if (lane == 0) raise_flag(CX_DEV_BAD_SLOT);
+                continue;
+            }
+            const int64_t blk = slot / g.block_size, off = slot % g.block_size;
+            const int64_t dst = g.tile(layer, blk, h) + off * D;
+            const int64_t src = (t * H + h) * D;
+            for (int64_t d = lane; d < D; d += 32) {
+                kp[dst + d] = Conv<P>::from_f(Conv<S>::to_f(kn[src + d]));
+                vp[dst + d] = Conv<P>::from_f(Conv<S>::to_f(vn[src + d]));
+            }
+        } else {
+            const int64_t c = t - n_tok;
+            const int64_t sb = cow_src[c], db = cow_dst[c], nv = cow_nv[c];
+            if (sb < 0 || sb >= g.n_blocks || db < 0 || db >= g.n_blocks || nv < 0 ||
+                nv > g.block_size) {
+                if (lane == 0) raise_flag(CX_DEV_BAD_BLOCK);
+                continue;
+            }
+            const int64_t nbytes = nv * D * (int64_t)sizeof(P);
+            copy_bytes(reinterpret_cast<char*>(kp + g.tile(layer, db, h)),
+                       reinterpret_cast<const char*>(kp + g.tile(layer, sb, h)), nbytes, lane, 32);
+            copy_bytes(reinterpret_cast<char*>(vp + g.tile(layer, db, h)),
+                       reinterpret_cast<const char*>(vp + g.tile(layer, sb, h)), nbytes, lane, 32);
+        }
+    }
+}
+
+// One warp per (token, head) row of the output.
+__global__ void __launch_bounds__(256) kv_gather_kernel(
+    const char* __restrict__ kp, const char* __restrict__ vp, PoolGeom g, int64_t layer,
+    int eb, const int32_t* __restrict__ table, int64_t n_tok, char* __restrict__ ko,
+    char* __restrict__ vo) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t H = g.n_kv_heads, D = g.head_dim;
+    const int64_t row_bytes = D * eb;
+    for (int64_t job = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+         job < n_tok * H; job += warps) {
+        const int64_t h = job % H, t = job / H;
+        const int64_t blk = table[t / g.block_size];
+        if (blk < 0 || blk >= g.n_blocks) {
+            if (lane == 0) raise_flag(CX_DEV_BAD_BLOCK);
+            continue;
+        }
+        const int64_t src = (g.tile(layer, blk, h) + (t % g.block_size) * D) * eb;
+        copy_bytes(ko + job * row_bytes, kp + src, row_bytes, lane, 32);
+        copy_bytes(vo + job * row_bytes, vp + src, row_bytes, lane, 32);
+    }
+}
+
+// One CTA per job = (pair, layer, head, K|V): slots [0, n_slots) of a tile.
+__global__ void __launch_bounds__(256) block_copy_kernel(
+    char* __restrict__ kp, char* __restrict__ vp, PoolGeom g, int eb,
+    const int32_t* __restrict__ src, const int32_t* __restrict__ dst, int64_t n,
+    int64_t n_slots) {
+    const int64_t H = g.n_kv_heads;
+    const int64_t n_jobs = n * g.n_layers * H * 2;
+    const int64_t nbytes = n_slots * g.head_dim * eb;
+    for (int64_t job = blockIdx.x; job < n_jobs; job += gridDim.x) {
+        int64_t r = job;
+        const int kv = (int)(r & 1);
+        r >>= 1;
+        const int64_t h = r % H;
+        r /= H;
+        const int64_t layer = r % g.n_layers;
+        const int64_t i = r / g.n_layers;
+        const int64_t sb = src[i], db = dst[i];
+        if (sb < 0 || sb >= g.n_blocks || db < 0 || db >= g.n_blocks) {
+            if (threadIdx.x == 0) raise_flag(CX_DEV_BAD_BLOCK);
+            continue;
+        }
+        char* base = kv ? vp : kp;
+        copy_bytes(base + g.tile(layer, db, h) * eb, base + g.tile(layer, sb, h) * eb, nbytes,
+                   threadIdx.x, blockDim.x);
+    }
+}
+
+static int check_pool(const cx_pool* p) {
+    if (!p) return fail(CX_ERR_SHAPE, "pool is NULL");
+    if (!p->k || !p->v) return fail(CX_ERR_SHAPE, "pool buffers are NULL");
+    if (p->n_layers <= 0 || p->n_blocks <= 0 || p->block_size <= 0 || p->n_kv_heads <= 0 ||
+        p->head_dim <= 0)
+        return fail(CX_ERR_SHAPE, "pool sizes must be positive");
+    if (elem_bytes(p->dtype) == 0) return fail(CX_ERR_DTYPE, "unknown pool dtype");
+    return CX_OK;
+}
+
+static int grid_for(int64_t work_items, int per_block) {
+    int64_t b = (work_items + per_block - 1) / per_block;
+    int64_t cap = (int64_t)num_sms() * 16;
+    if (cap <= 0) cap = 2048;
+    if (b > cap) b = cap;
+    return (int)(b < 1 ? 1 : b);
+}
+
+template <typename S, typename P>
+static void launch_append(const cx_pool* p, int64_t layer, const void* k, const void* v,
+                          const int64_t* slots, int64_t n_tok, const int32_t* cs,
+                          const int32_t* cd, const int32_t* cn, int64_t n_cow, cudaStream_t st) {
+    const int64_t jobs = (n_tok + n_cow) * p->n_kv_heads;
+    kv_append_kernel<S, P><<<grid_for(jobs, 8), 256, 0, st>>>(
+        static_cast<P*>(p->k), static_cast<P*>(p->v), geom_of(p), layer,
+        static_cast<const S*>(k), static_cast<const S*>(v), slots, n_tok, cs, cd, cn, n_cow);
+}
+
+template <typename P>
+static int dispatch_append_src(int32_t sdt, const cx_pool* p, int64_t layer, const void* k,
+                               const void* v, const int64_t* slots, int64_t n_tok,
+                               const int32_t* cs, const int32_t* cd, const int32_t* cn,
+                               int64_t n_cow, cudaStream_t st) {
+    switch (sdt) {
+        case CX_F32: launch_append<float, P>(p, layer, k, v, slots, n_tok, cs, cd, cn, n_cow, st); break;
+        case CX_BF16: launch_append<__nv_bfloat16, P>(p, layer, k, v, slots, n_tok, cs, cd, cn, n_cow, st); break;
+        case CX_F16: launch_append<__half, P>(p, layer, k, v, slots, n_tok, cs, cd, cn, n_cow, st); break;
+        default: return fail(CX_ERR_DTYPE, "cx_kv_append: unknown source dtype");
+    }
+    return check_launch("kv_append_kernel");
+}
+
+}  // namespace cx
+
+extern "C" {
+
+int cx_kv_append(const cx_pool* pool, int64_t layer, const void* k_new, const void* v_new,
+                 int32_t src_dtype, const int64_t* slot_mapping, int64_t n_tokens,
+                 const int32_t* cow_src, const int32_t* cow_dst, const int32_t* cow_n_valid,
+                 int64_t n_cow, void* stream) {
+    using namespace cx;
+    int rc = check_pool(pool);
+    if (rc) return rc;
+    if (layer < 0 || layer >= pool->n_layers)
+        return fail(CX_ERR_RANGE, "cx_kv_append: layer out of range");
+    if (n_tokens < 0 || n_cow < 0) return fail(CX_ERR_SHAPE, "cx_kv_append: negative count");
+    if (n_tokens > 0 && (!k_new || !v_new || !slot_mapping))
+        return fail(CX_ERR_SHAPE, "cx_kv_append: NULL token arrays");
+    if (n_cow > 0 && (!cow_src || !cow_dst || !cow_n_valid))
+        return fail(CX_ERR_SHAPE, "cx_kv_append: NULL copy-on-write arrays");
+    if (n_tokens == 0 && n_cow == 0) return CX_OK;
+    cudaStream_t st = as_stream(stream);
+    switch (pool->dtype) {
+        case CX_F32: return dispatch_append_src<float>(src_dtype, pool, layer, k_new, v_new, slot_mapping, n_tokens, cow_src, cow_dst, cow_n_valid, n_cow, st);
+        case CX_BF16: return dispatch_append_src<__nv_bfloat16>(src_dtype, pool, layer, k_new, v_new, slot_mapping, n_tokens, cow_src, cow_dst, cow_n_valid, n_cow, st);
+        case CX_F16: return dispatch_append_src<__half>(src_dtype, pool, layer, k_new, v_new, slot_mapping, n_tokens, cow_src, cow_dst, cow_n_valid, n_cow, st);
+        default: return fail(CX_ERR_DTYPE, "cx_kv_append: unknown pool dtype");
+    }
+}
+
+int cx_kv_gather(const cx_pool* pool, int64_t layer, const int32_t* block_table,
+                 int64_t n_tokens, void* k_out, void* v_out, void* stream) {
+    using namespace cx;
+    int rc = check_pool(pool);
+    if (rc) return rc;
+    if (layer < 0 || layer >= pool->n_layers)
+        return fail(CX_ERR_RANGE, "cx_kv_gather: layer out of range");
+    if (n_tokens < 0) return fail(CX_ERR_SHAPE, "cx_kv_gather: negative n_tokens");
+    if (n_tokens == 0) return CX_OK;
+    if (!block_table || !k_out || !v_out) return fail(CX_ERR_SHAPE, "cx_kv_gather: NULL array");
+    const int eb = elem_bytes(pool->dtype);
+    kv_gather_kernel<<<grid_for(n_tokens * pool->n_kv_heads, 8), 256, 0, as_stream(stream)>>>(
+        static_cast<const char*>(pool->k), static_cast<const char*>(pool->v), geom_of(pool), layer,
+        eb, block_table, n_tokens, static_cast<char*>(k_out), static_cast<char*>(v_out));
+    return check_launch("kv_gather_kernel");
+}
+
+int cx_block_copy(const cx_pool* pool, const int32_t* src, const int32_t* dst, int64_t n,
+                  int64_t n_slots, void* stream) {
+    using namespace cx;
+    int rc = check_pool(pool);
+    if (rc) return rc;
+    if (n < 0 || n_slots < 0 || n_slots > pool->block_size)
+        return fail(CX_ERR_SHAPE, "cx_block_copy: bad n or n_slots");
+    if (n == 0 || n_slots == 0) return CX_OK;
+    if (!src || !dst) return fail(CX_ERR_SHAPE, "cx_block_copy: NULL id arrays");
+    const int64_t jobs = n * pool->n_layers * pool->n_kv_heads * 2;
+    block_copy_kernel<<<grid_for(jobs, 1), 256, 0, as_stream(stream)>>>(
+        static_cast<char*>(pool->k), static_cast<char*>(pool->v), geom_of(pool),
+        elem_bytes(pool->dtype), src, dst, n, n_slots);
+    return check_launch("block_copy_kernel");
+}
+
+}  // extern "C"

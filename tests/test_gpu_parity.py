@@ -1,0 +1,357 @@
+"""GPU parity: every libcxkv kernel against the CPU oracle / reference goldens.
+
+Tolerances (written here, used throughout):
+* fp32 pools — max |out - ref| <= 1e-5 (the reference's own flash-vs-naive bar);
+* bf16 pools — max |out - ref| <= 2e-2 * max |ref| per sequence;
+* append / gather / block copy / tables / slots — bit-exact.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_cases import BF16_RTOL, F32_ATOL, PagedCase, bf16_round
+from golden import cases as gcases
+from replay import GOLDEN, load_json
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _clean_flags():
+    from chenxing_b200 import _lib
+    _lib.device_flags(clear=True)
+    yield
+    flags = _lib.device_flags(clear=True)
+    assert flags == 0, f"device error flags raised: {_lib.describe_flags(flags)}"
+
+
+# ---------------------------------------------------------------------------
+# drop-in API: the reference's own radix_kv / attention tests, on the GPU
+# ---------------------------------------------------------------------------
+def test_reference_write_read_roundtrip():
+    """tests/test_radix_kv.py:82-90 of the reference."""
+    from chenxing_b200 import RadixPagedKVCache
+    c = RadixPagedKVCache(n_blocks=4, block_size=2, n_layers=1, n_kv_heads=2, head_dim=4)
+    bid = c.alloc_block()
+    rng = np.random.default_rng(0)
+    k = rng.standard_normal((2, 2, 4)).astype(np.float32)
+    v = rng.standard_normal((2, 2, 4)).astype(np.float32)
+    c.write_layer([bid], 0, 0, k, v)
+    kr, vr = c.read_layer([bid], 2, 0)
+    assert isinstance(kr, np.ndarray) and np.array_equal(kr, k) and np.array_equal(vr, v)
+
+
+def test_reference_write_beyond_table_raises():
+    """tests/test_radix_kv.py:93-96 of the reference."""
+    from chenxing_b200 import RadixPagedKVCache
+    c = RadixPagedKVCache(n_blocks=8, block_size=2, n_layers=1, n_kv_heads=2, head_dim=4)
+    with pytest.raises(ValueError):
+        c.write_layer([0], 0, 0, np.zeros((4, 2, 4)), np.zeros((4, 2, 4)))
+
+
+def test_read_layer_edge_cases_match_oracle():
+    from chenxing_b200 import RadixPagedKVCache
+    from oracle.radix_kv import OraclePagedKVCache
+    rng = np.random.default_rng(4)
+    for dtype, odt in (("bfloat16", gcases.BF16), (np.float32, np.float32)):
+        c = RadixPagedKVCache(6, 4, 2, 3, 5, dtype=dtype)
+        o = OraclePagedKVCache(6, 4, 2, 3, 5, dtype=odt)
+        table = [4, 1, 5]
+        k = rng.standard_normal((11, 3, 5)).astype(np.float32)
+        v = rng.standard_normal((11, 3, 5)).astype(np.float32)
+        for layer in (0, 1):
+            c.write_layer(table, 0, layer, k, v)
+            o.write_layer(table, 0, layer, k, v)
+        for n in (0, 1, 4, 7, 11, 99):
+            for layer in (0, 1):
+                a, b = c.read_layer(table, n, layer), o.read_layer(table, n, layer)
+                assert a[0].shape == b[0].shape
+                assert np.array_equal(np.asarray(a[0]).view(np.uint8), np.asarray(b[0]).view(np.uint8))
+                assert np.array_equal(np.asarray(a[1]).view(np.uint8), np.asarray(b[1]).view(np.uint8))
+        e = c.read_layer([], 5, 0)
+        assert e[0].shape == (0, 3, 5)
+
+
+def test_pool_view_has_reference_axis_order():
+    from chenxing_b200 import RadixPagedKVCache
+    c = RadixPagedKVCache(3, 4, 2, 2, 8)
+    assert tuple(c.k_pool.shape) == (2, 3, 4, 2, 8)
+    k = np.arange(2 * 2 * 8, dtype=np.float32).reshape(2, 2, 8)
+    c.write_layer([2], 1, 1, k, k)
+    got = c.k_pool[1, 2, 1:3].cpu().numpy()
+    assert np.array_equal(got, k)
+
+
+def test_dense_attention_matches_reference_golden():
+    from chenxing_b200 import CausalMask, flash_attention, naive_attention
+    out = np.load(os.path.join(GOLDEN, "attention.npz"))
+    meta = {m["name"]: m["digest"] for m in load_json("attention_cases.json")}
+    for c in gcases.attention_cases():
+        assert gcases.case_digest(c) == meta[c["name"]]
+        if c["mask"] == "causal":
+            m = CausalMask(c["window"])
+        elif c["mask"] == "explicit":
+            m = c["explicit"]
+        else:
+            m = None
+        fn = flash_attention if c["use"] == "flash" else naive_attention
+        got = fn(c["q"], c["k"], c["v"], m, c["scale"])
+        assert isinstance(got, np.ndarray) and got.dtype == np.float32
+        np.testing.assert_allclose(got, out[c["name"]], rtol=0, atol=F32_ATOL, err_msg=c["name"])
+
+
+def test_dense_attention_torch_io_and_errors():
+    from chenxing_b200 import CausalMask, flash_attention, gqa_expand
+    q = torch.randn(1, 4, 3, 8, device="cuda")
+    k = torch.randn(1, 3, 5, 8, device="cuda")
+    with pytest.raises(ValueError):
+        flash_attention(q, k, k)
+    k = torch.randn(1, 2, 5, 8, device="cuda")
+    o = flash_attention(q, k, k, CausalMask())
+    assert o.is_cuda and o.dtype == torch.float32 and o.shape == (1, 4, 3, 8)
+    with pytest.raises(ValueError):
+        flash_attention(q, k, k, np.ones((2, 2), dtype=bool))
+    e = gqa_expand(np.arange(12, dtype=np.float32).reshape(1, 2, 3, 2), 2, 4)
+    assert e.shape == (1, 4, 3, 2) and np.array_equal(e[0, 1], e[0, 0])
+
+
+# ---------------------------------------------------------------------------
+# cfg1 (fp32 pool, generic kernel) and the bf16 golden (tensor-core kernel)
+# ---------------------------------------------------------------------------
+def test_cfg1_decode_run_matches_reference_golden():
+    from chenxing_b200 import PagedBatch, RadixPagedKVCache, slot_mapping
+    from chenxing_b200.workloads import cfg1
+    g = np.load(os.path.join(GOLDEN, "paged_cfg1.npz"))
+    wl, data = cfg1(seed=0)
+    cache = RadixPagedKVCache(wl.n_blocks, wl.block_size, 1, wl.n_kv_heads, wl.head_dim,
+                              host_io=False)
+    ctx = wl.ctx_lens.copy()
+    for b in range(wl.batch):     # prefill through the drop-in write_layer
+        cache.write_layer(wl.block_tables[b], 0, 0, data["k_pre"][b], data["v_pre"][b])
+    for s in range(wl.steps):
+        slots = slot_mapping(wl.block_tables, ctx, [1] * wl.batch, wl.block_size)
+        cache.append_batch(0, data["k"][s], data["v"][s], slots)
+        ctx += 1
+        batch = PagedBatch(cache, wl.block_tables, ctx, n_q_heads=wl.n_q_heads)
+        out = cache.decode_batch(0, data["q"][s], batch).cpu().numpy()
+        key = f"out_step{s}"
+        if key in g.files:
+            np.testing.assert_allclose(out, g[key], rtol=0, atol=F32_ATOL, err_msg=key)
+    assert np.array_equal(ctx, g["final_ctx"])
+    # the pool holds exactly what the reference pool holds (same bytes)
+    kp = cache.k_pool.cpu().numpy()
+    vp = cache.v_pool.cpu().numpy()
+    assert gcases.digest(kp, vp).encode() == g["pool_digest"].tobytes()
+
+
+def test_bf16_decode_matches_reference_golden():
+    from chenxing_b200 import PagedBatch, RadixPagedKVCache, slot_mapping
+    g = np.load(os.path.join(GOLDEN, "paged_bf16.npz"))
+    wl, ks, vs, qs = gcases.paged_bf16_inputs()
+    cache = RadixPagedKVCache(wl.n_blocks, wl.block_size, 1, wl.n_kv_heads, wl.head_dim,
+                              dtype=gcases.BF16, host_io=False)
+    ctx = np.array([len(k) for k in ks])
+    for b in range(wl.batch):
+        cache.append_batch(0, ks[b], vs[b], slot_mapping([wl.block_tables[b]], [0], [ctx[b]], 16))
+    bits = [cache.read_layer(wl.block_tables[b], int(ctx[b]), 0)[0].view(torch.int16).cpu().numpy()
+            .view(np.uint16) for b in range(wl.batch)]
+    assert gcases.digest(*bits).encode() == g["kbits_digest"].tobytes()
+    batch = PagedBatch(cache, wl.block_tables, ctx, n_q_heads=wl.n_q_heads)
+    out = cache.decode_batch(0, np.stack(qs), batch).cpu().numpy()
+    for b in range(wl.batch):
+        ref = g["out"][b]
+        assert np.abs(out[b] - ref).max() <= BF16_RTOL * np.abs(ref).max()
+
+
+# ---------------------------------------------------------------------------
+# tensor-core decode / verify against the oracle, seeded random shapes
+# ---------------------------------------------------------------------------
+DECODE_CTX = [1, 15, 16, 17, 31, 250, 1000, 4097, 33]
+
+
+@pytest.mark.parametrize("d", [128, 64])
+@pytest.mark.parametrize("hq,hk", [(32, 8), (8, 8), (16, 2)])
+@pytest.mark.parametrize("q_dtype", [torch.float32, torch.bfloat16])
+def test_decode_bf16_matches_oracle(d, hq, hk, q_dtype):
+    case = PagedCase(hq=hq, hk=hk, d=d, ctx=DECODE_CTX, q_dtype=q_dtype, seed=d + hq + hk)
+    case.check(case.run(), rtol=BF16_RTOL)
+
+
+@pytest.mark.parametrize("window", [1, 16, 37, 300])
+def test_decode_sliding_window(window):
+    case = PagedCase(hq=32, hk=8, d=128, ctx=DECODE_CTX, window=window, seed=window)
+    case.check(case.run(), rtol=BF16_RTOL)
+
+
+def test_decode_long_context_splits_across_ctas():
+    # few sequences, long contexts: every (sequence, head) range is split over
+    # many CTAs and finished by the last-arriving one
+    case = PagedCase(hq=32, hk=8, d=128, ctx=[20000, 3, 9000], seed=11, q_scale=3.0)
+    case.check(case.run(), rtol=BF16_RTOL)
+
+
+def test_decode_empty_and_single_token_sequences():
+    case = PagedCase(hq=32, hk=8, d=128, ctx=[0, 1, 0, 64, 0], seed=5)
+    out = case.run()
+    case.check(out, rtol=BF16_RTOL)
+    assert np.all(out[[0, 2, 4]] == 0)
+
+
+def test_decode_plan_reused_across_layers():
+    from chenxing_b200 import slot_mapping
+    case = PagedCase(hq=32, hk=8, d=128, ctx=[300, 700, 5, 1200], n_layers=3, layer=0, seed=2)
+    # fill layers 1 and 2 with other values, attend all three with one plan
+    rng = np.random.default_rng(9)
+    ks, vs = {0: case.k}, {0: case.v}
+    slots = slot_mapping(case.tables, [0] * 4, case.ctx, 16)
+    for layer in (1, 2):
+        k = rng.standard_normal(case.k.shape).astype(np.float32)
+        v = rng.standard_normal(case.v.shape).astype(np.float32)
+        case.cache.append_batch(layer, k, v, slots)
+        ks[layer], vs[layer] = bf16_round(k), bf16_round(v)
+    batch = case.batch()
+    for layer in (0, 1, 2):
+        out = case.cache.decode_batch(layer, case.q_dev, batch).cpu().numpy()
+        assert not batch.needs_plan
+        case.k, case.v = ks[layer], vs[layer]
+        case.check(out, rtol=BF16_RTOL)
+
+
+@pytest.mark.parametrize("gamma", [1, 4, 8, 15])
+@pytest.mark.parametrize("window", [None, 4096, 40])
+def test_verify_bf16_matches_oracle(gamma, window):
+    ctx = [gamma + 1, 100, 2048, 5000, 777, gamma + 17]
+    case = PagedCase(hq=32, hk=8, d=128, ctx=ctx, q_lens=[gamma + 1] * len(ctx),
+                     window=window, seed=gamma * 7 + (window or 0))
+    case.check(case.run(), rtol=BF16_RTOL)
+
+
+def test_verify_ragged_query_lengths():
+    ctx = [9, 300, 64, 1000, 5]
+    case = PagedCase(hq=16, hk=4, d=64, ctx=ctx, q_lens=[9, 1, 16, 3, 5], seed=3)
+    case.check(case.run(), rtol=BF16_RTOL)
+
+
+def test_fp32_pool_paged_decode_and_verify_exact():
+    case = PagedCase(hq=8, hk=2, d=64, ctx=[64, 511, 1, 130], dtype="float32", seed=1)
+    case.check(case.run(), atol=F32_ATOL)
+    case = PagedCase(hq=8, hk=2, d=64, ctx=[64, 511, 9, 130], q_lens=[5, 5, 9, 1],
+                     dtype="float32", window=50, seed=2)
+    case.check(case.run(), atol=F32_ATOL)
+
+
+def test_odd_shapes_use_generic_path():
+    # head_dim 40 and block size 8 are outside the tensor-core kernel
+    case = PagedCase(hq=6, hk=3, d=40, ctx=[3, 90, 17], bs=8, seed=8)
+    case.check(case.run(), rtol=BF16_RTOL)
+
+
+# ---------------------------------------------------------------------------
+# append / copy-on-write / block copy: bit-exact
+# ---------------------------------------------------------------------------
+def test_append_rounding_and_skips_bit_exact():
+    from chenxing_b200 import RadixPagedKVCache
+    rng = np.random.default_rng(0)
+    c = RadixPagedKVCache(8, 16, 2, 4, 128, dtype="bfloat16", host_io=False)
+    k = (rng.standard_normal((10, 4, 128)) * 3).astype(np.float32)
+    v = (rng.standard_normal((10, 4, 128)) * 3).astype(np.float32)
+    slots = np.array([5, 17, -1, 100, 0, 127, 64, 65, -1, 33], dtype=np.int64)
+    c.append_batch(1, k, v, slots)
+    kp = c.k_pool[1].reshape(-1, 4, 128).float().cpu().numpy()
+    vp = c.v_pool[1].reshape(-1, 4, 128).float().cpu().numpy()
+    for t, s in enumerate(slots):
+        if s < 0:
+            continue
+        assert np.array_equal(kp[s], bf16_round(k[t])) and np.array_equal(vp[s], bf16_round(v[t]))
+    written = set(int(s) for s in slots if s >= 0)
+    for s in range(128):
+        if s not in written:
+            assert not kp[s].any() and not vp[s].any()
+    assert not c.k_pool[0].any()
+
+
+def test_cow_tail_and_block_copy_bit_exact():
+    from chenxing_b200 import RadixPagedKVCache
+    rng = np.random.default_rng(1)
+    c = RadixPagedKVCache(10, 16, 3, 2, 64, dtype="bfloat16", host_io=False)
+    shared = [c.alloc_block() for _ in range(2)]       # prefix of 16 + 5 tokens
+    k = rng.standard_normal((21, 2, 64)).astype(np.float32)
+    for layer in range(3):
+        c.write_layer(shared, 0, layer, k + layer, k - layer)
+    before = c.k_pool.clone()
+    table = list(shared)
+    res = c.cow_tail(table, 21, lambda b: b in shared)
+    assert res is not None and res[0] == shared[1] and res[2] == 5 and table[1] == res[1]
+    assert torch.equal(c.k_pool[:, shared[1]], before[:, shared[1]])     # source untouched
+    assert torch.equal(c.k_pool[:, res[1], :5], before[:, shared[1], :5])
+    assert torch.equal(c.v_pool[:, res[1], :5], c.v_pool[:, shared[1], :5])
+    # appending the next token now lands in the private block only
+    nk = rng.standard_normal((1, 2, 64)).astype(np.float32)
+    c.write_layer(table, 21, 0, nk, nk)
+    assert torch.equal(c.k_pool[0, shared[1]], before[0, shared[1]])
+    # whole-block copies across all layers
+    dst = [c.alloc_block(), c.alloc_block()]
+    c.copy_blocks(shared, dst)
+    assert torch.equal(c.k_pool[:, dst], c.k_pool[:, shared])
+    assert torch.equal(c.v_pool[:, dst], c.v_pool[:, shared])
+
+
+def test_fused_cow_in_append_bit_exact():
+    from chenxing_b200 import RadixPagedKVCache
+    rng = np.random.default_rng(2)
+    c = RadixPagedKVCache(6, 16, 2, 2, 128, dtype="bfloat16", host_io=False)
+    k = rng.standard_normal((16, 2, 128)).astype(np.float32)
+    c.write_layer([3], 0, 1, k, k)
+    # privatise block 3 (7 valid slots) into block 4 while appending slot 4*16+7
+    nk = rng.standard_normal((1, 2, 128)).astype(np.float32)
+    c.append_batch(1, nk, nk, np.array([4 * 16 + 7]), cow=(np.array([3]), np.array([4]), np.array([7])))
+    assert torch.equal(c.k_pool[1, 4, :7], c.k_pool[1, 3, :7])
+    assert np.array_equal(c.k_pool[1, 4, 7].float().cpu().numpy(), bf16_round(nk[0]))
+    assert not c.k_pool[1, 4, 8:].any() and not c.k_pool[0, 4].any()
+
+
+# ---------------------------------------------------------------------------
+# device-side range checks: flagged, never faulting
+# ---------------------------------------------------------------------------
+def test_device_range_checks_raise_flags():
+    from chenxing_b200 import PagedBatch, RadixPagedKVCache, _lib
+    c = RadixPagedKVCache(4, 16, 1, 8, 128, dtype="bfloat16", host_io=False)
+    x = torch.zeros((1, 8, 128), device="cuda")
+    c.append_slots(0, x, x, torch.tensor([4 * 16 + 3], device="cuda"))
+    assert _lib.device_flags(clear=True) & 1
+    b = PagedBatch(c, [[0, 1]], [20], n_q_heads=32)
+    b.block_tables[0, 1] = 9                      # bypass host validation
+    c.decode_batch(0, torch.zeros((1, 32, 128), device="cuda"), b)
+    assert _lib.device_flags(clear=True) & 2
+
+
+# ---------------------------------------------------------------------------
+# cfg2 at full size (64 sequences, 1k-8k tokens): sampled oracle rows plus
+# size-independent properties
+# ---------------------------------------------------------------------------
+def test_cfg2_full_size_properties():
+    rng = np.random.default_rng(0)
+    ctx = rng.integers(1024, 8193, size=64)
+    case = PagedCase(hq=32, hk=8, d=128, ctx=ctx, seed=0, q_scale=1 / np.sqrt(128),
+                     kv_scale=1 / np.sqrt(128))
+    out = case.run()
+    # (1) sampled sequences against the oracle
+    refs = case.oracle()
+    starts = np.concatenate([[0], np.cumsum(case.q_lens)])
+    for b in (0, 17, 63):
+        ref = refs[b]
+        assert np.abs(out[starts[b]:starts[b + 1]] - ref).max() <= BF16_RTOL * np.abs(ref).max()
+    # (2) same K/V relocated to other physical blocks -> bit-identical output
+    case2 = PagedCase(hq=32, hk=8, d=128, ctx=ctx, seed=0, q_scale=1 / np.sqrt(128),
+                      kv_scale=1 / np.sqrt(128), spare_blocks=301)
+    assert case2.tables != case.tables
+    assert np.array_equal(case2.run(), out)
+    # (3) constant V rows -> output equals that row exactly (convex combination)
+    ones = np.full_like(case.v, 0.375)
+    from chenxing_b200 import slot_mapping
+    slots = slot_mapping(case.tables, [0] * len(ctx), case.ctx, 16)
+    case.cache.append_batch(0, case.k, ones, slots)
+    out3 = case.run()
+    assert np.abs(out3 - 0.375).max() <= 2e-3
