@@ -1,28 +1,31 @@
 // Paged flash-decode / multi-query verify over a bf16 pool with 16-token
 // blocks and head_dim 64 or 128 (sm_100a).
 //
-// Work decomposition ("units"): one unit = one 16-token block of one KV head
-// of one sequence.  All units of a call are laid out as
-//     for b in sequences: for h in kv heads: for j in the sequence's blocks
-// and split into equal contiguous chunks, one chunk per persistent CTA, so
-// every SM streams the same number of bytes whatever the context-length mix.
-// A chunk may start or end inside a (sequence, head) range; such a range is
+// Work decomposition ("units"): one unit = one 16-token block of a group of
+// HG consecutive KV heads of one sequence.  Because the pool stores the
+// heads of a block next to each other ([layer][block][head][16][D]), the K
+// (and the V) data of a unit is one contiguous HG x 4 KB run, fetched by two
+// TMA tile loads (the two 128-byte column halves, 128-byte swizzle).  All
+// units of a call are laid out as
+//     for b in sequences: for g in head groups: for j in the sequence's blocks
+// and split into equal contiguous chunks, one per persistent CTA, so every SM
+// streams the same number of bytes whatever the context-length mix.  A chunk
+// may start or end inside a (sequence, head group) range; such a range is
 // finished by whichever CTA arrives last at its counter (atomic ticket, no
 // waiting), which merges the per-CTA partial softmax states from the
-// workspace (log-sum-exp merge) and writes the final row.
+// workspace (log-sum-exp merge) and writes the final rows.
 //
-// Inside a CTA: warp NCW is the producer.  Its lanes fetch 32 block ids of
-// the table at a time; lane 0 issues, per unit, TMA tile loads (no multicast)
-// of the 16 x D K tile and V tile into a STAGES-deep shared-memory ring,
-// completing on a per-stage mbarrier.  The TMA writes the 128-byte swizzled
-// layout, so the ldmatrix reads below are bank-conflict free.  Consumer
-// warps are indexed (mt, ks): mt picks 16 packed query rows (row = query
-// token * G + head-in-group), ks picks every KS-th unit.  Per unit a consumer
-// computes S = Q K^T and O += P V with mma.sync m16n8k16 (bf16 in, fp32
-// accumulate) and keeps the online softmax (running max m, denominator l,
-// rescaled O) in registers, reducing row maxima across each lane quad with
-// warp shuffles.  At the end of a (sequence, head) range the KS states are
-// merged through shared memory.  Every wait is bounded (CX_DEV_WAIT_TIMEOUT).
+// Inside a CTA: the last warp is the producer.  Its lanes fetch 32 block ids
+// of the table at a time; lane 0 issues the TMA loads (no multicast) of each
+// unit into a ring of shared-memory stages, completing on per-stage
+// mbarriers.  Consumer warps are indexed (hh, mt, ks): head hh of the group,
+// 16 packed query rows mt (row = query token * G + head-in-group), and key
+// slice ks (every KS-th unit).  Per unit a consumer computes S = Q K^T and
+// O += P V with mma.sync m16n8k16 (bf16 in, fp32 accumulate) and keeps the
+// online softmax (running max m, denominator l, rescaled O) in registers,
+// reducing row maxima across each lane quad with warp shuffles.  Key slices
+// (KS > 1) are merged through shared memory at the end of a range.  Every
+// wait is bounded and reports CX_DEV_WAIT_TIMEOUT instead of hanging.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -35,7 +38,9 @@ namespace cx {
 constexpr int kBlockTok = 16;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
 constexpr int kPlanMagic = 0x43584b56;                       // "CXKV"
-constexpr int kMinUnitsPerCta = 8;
+constexpr int kMinUnitsPerCta = 4;
+constexpr int kConsumerWarps = 8;
+constexpr size_t kSmemBudget = 227 * 1024;
 
 struct MmaParams {
     const int32_t* tables;
@@ -43,20 +48,35 @@ struct MmaParams {
     const int32_t* ctx_lens;
     const int32_t* q_start;  // NULL: decode, one query row per sequence
     int32_t batch, hk, hq, group, max_q, rows;
+    int32_t hg, n_groups;    // heads per unit, head groups per sequence
     int32_t n_blocks, layer, window;
+    int32_t stages, stage_bytes;
     float scale_log2;
     const void* q;
     float* out;
-    int32_t* plan;       // [16] header: W, chunk, P_eff, magic, batch, hk
+    int32_t* plan;       // [16] header: W, chunk, P_eff, magic, batch, n_groups
     int32_t* seq_start;  // [batch + 1] first unit of each sequence
     int32_t* blk_lo;     // [batch] first block attended (sliding window)
-    int32_t* counters;   // [batch * hk] merge tickets, zero between calls
-    float* partials;     // [(P + batch*hk)][rows][D + 2]
+    int32_t* counters;   // [batch * n_groups] merge tickets, zero between calls
+    float* partials;     // [(P + batch*n_groups)][hg][rows][D + 2]
 };
 
 // ---------------------------------------------------------------------------
 // plan: unit prefix sums and the chunking (one CTA of 1024 threads)
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ int plan_units(const MmaParams& p, int b, int* lo_out) {
+    int ctx = p.ctx_lens[b];
+    const int sq = p.q_start ? p.q_start[b + 1] - p.q_start[b] : 1;
+    const int cap = (int)(p.table_stride * kBlockTok);
+    ctx = min(max(ctx, 0), cap);
+    int lo_tok = 0;
+    if (p.window > 0) lo_tok = max(0, ctx - sq - p.window + 1);
+    const int lo = lo_tok / kBlockTok;
+    const int hi = (ctx + kBlockTok - 1) / kBlockTok;
+    *lo_out = lo;
+    return (ctx > 0 && hi > lo) ? (hi - lo) : 0;
+}
+
 __global__ void __launch_bounds__(1024) paged_plan_kernel(MmaParams p, int grid) {
     __shared__ long long s_part[1024];
     const int t = threadIdx.x, B = p.batch;
@@ -64,22 +84,14 @@ __global__ void __launch_bounds__(1024) paged_plan_kernel(MmaParams p, int grid)
     const int b0 = t * per, b1 = min(B, b0 + per);
     long long local = 0;
     for (int b = b0; b < b1; ++b) {
-        int ctx = p.ctx_lens[b];
+        const int ctx = p.ctx_lens[b];
         const int sq = p.q_start ? p.q_start[b + 1] - p.q_start[b] : 1;
-        const long long cap = p.table_stride * (long long)kBlockTok;
-        if (ctx < 0) ctx = 0;
-        if (ctx > cap) {
-            raise_flag(CX_DEV_TABLE_OVERRUN);
-            ctx = (int)cap;
-        }
+        if (ctx > p.table_stride * kBlockTok) raise_flag(CX_DEV_TABLE_OVERRUN);
         // an empty sequence (ctx == 0) is allowed and yields zero rows
         if (sq > p.max_q || sq < 0 || (ctx > 0 && sq > ctx)) raise_flag(CX_DEV_BAD_QLEN);
-        int lo_tok = 0;
-        if (p.window > 0) lo_tok = max(0, ctx - sq - p.window + 1);
-        const int lo = lo_tok / kBlockTok;
-        const int hi = (ctx + kBlockTok - 1) / kBlockTok;
+        int lo;
+        local += (long long)plan_units(p, b, &lo) * p.n_groups;
         p.blk_lo[b] = lo;
-        local += (ctx > 0 && hi > lo) ? (long long)(hi - lo) * p.hk : 0;
     }
     s_part[t] = local;
     __syncthreads();
@@ -92,11 +104,10 @@ __global__ void __launch_bounds__(1024) paged_plan_kernel(MmaParams p, int grid)
     long long run = s_part[t] - local;  // exclusive prefix
     for (int b = b0; b < b1; ++b) {
         p.seq_start[b] = (int)run;
-        int ctx = min(max(p.ctx_lens[b], 0), (int)(p.table_stride * kBlockTok));
-        const int hi = (ctx + kBlockTok - 1) / kBlockTok;
-        run += (ctx > 0 && hi > p.blk_lo[b]) ? (long long)(hi - p.blk_lo[b]) * p.hk : 0;
+        int lo;
+        run += (long long)plan_units(p, b, &lo) * p.n_groups;
     }
-    for (int i = t; i < B * p.hk; i += 1024) p.counters[i] = 0;
+    for (int i = t; i < B * p.n_groups; i += 1024) p.counters[i] = 0;
     if (t == 1023) {
         long long W = s_part[1023];
         if (W > (1ll << 30)) {
@@ -112,7 +123,7 @@ __global__ void __launch_bounds__(1024) paged_plan_kernel(MmaParams p, int grid)
         p.plan[1] = (int)chunk;
         p.plan[2] = W > 0 ? (int)((W + chunk - 1) / chunk) : 0;
         p.plan[4] = B;
-        p.plan[5] = p.hk;
+        p.plan[5] = p.n_groups;
         __threadfence();
         p.plan[3] = kPlanMagic;
     }
@@ -122,20 +133,20 @@ __global__ void __launch_bounds__(1024) paged_plan_kernel(MmaParams p, int grid)
 // main kernel
 // ---------------------------------------------------------------------------
 struct Seg {
-    int b, h, j0, cnt, nb;
+    int b, g, j0, cnt, nb;
     bool whole;
 };
 
-// Walks the (sequence, head) ranges covered by the CTA's unit interval.
+// Walks the (sequence, head group) ranges covered by the CTA's unit interval.
 struct SegCursor {
-    int u, u_end, b, batch, hk;
+    int u, u_end, b, batch, ng;
     const int32_t* seq_start;
     const int32_t* blk_lo;
     __device__ void init(int u0, int u1, const MmaParams& p) {
         u = u0;
         u_end = u1;
         batch = p.batch;
-        hk = p.hk;
+        ng = p.n_groups;
         seq_start = p.seq_start;
         blk_lo = p.blk_lo;
         int lo = 0, hi = batch;  // largest b with seq_start[b] <= u0
@@ -149,12 +160,11 @@ struct SegCursor {
         if (u >= u_end) return false;
         while (b < batch && seq_start[b + 1] <= u) ++b;
         if (b >= batch) return false;
-        const int n_units = seq_start[b + 1] - seq_start[b];
-        const int nb = n_units / hk;
+        const int nb = (seq_start[b + 1] - seq_start[b]) / ng;
         const int local = u - seq_start[b];
         s.b = b;
-        s.h = local / nb;
-        const int jo = local - s.h * nb;
+        s.g = local / nb;
+        const int jo = local - s.g * nb;
         s.cnt = min(nb - jo, u_end - u);
         s.j0 = blk_lo[b] + jo;
         s.nb = nb;
@@ -163,13 +173,6 @@ struct SegCursor {
         return true;
     }
 };
-
-template <int D>
-__device__ __forceinline__ uint32_t swz(int t, int d) {
-    // byte offset of (token t, dim d [multiple of 8]) in a TMA SWIZZLE_128B
-    // tile made of D/64 boxes of 16 rows x 128 bytes
-    return (uint32_t)((d >> 6) * (kBlockTok * 128) + t * 128 + ((((d & 63) >> 3) ^ (t & 7)) << 4));
-}
 
 template <typename QT> struct QLoad;
 template <> struct QLoad<float> {
@@ -183,33 +186,52 @@ template <> struct QLoad<__nv_bfloat16> {
     }
 };
 
-template <int D, int MT, int KS, int STAGES>
+template <int D, int MT, int HG>
 struct MmaCfg {
-    static constexpr int NCW = MT * KS;             // consumer warps
-    static constexpr int THREADS = (NCW + 1) * 32;  // + producer warp
-    static constexpr int TILE = kBlockTok * D * 2;  // bytes of one K (or V) tile
-    static constexpr int STAGE = 2 * TILE;
-    static constexpr int NT = D / 8;    // n-tiles of the output
+    static constexpr int KS = (HG * MT >= kConsumerWarps) ? 1 : kConsumerWarps / (HG * MT);
+    static constexpr int NCW = HG * MT * KS;           // consumer warps
+    static constexpr int THREADS = (NCW + 1) * 32;     // + producer warp
+    static constexpr int HALF_BOX = kBlockTok * 128;   // one head, 16 rows x 128 B
+    static constexpr int TILES = HG * kBlockTok * D * 2;  // K (or V) bytes of a unit
+    static constexpr int STAGE = 2 * TILES;
+    static constexpr int NT = D / 8;     // n-tiles of the output
     static constexpr int KSTEP = D / 16;
-    static size_t smem_bytes(int rows) {
-        return 1024 + (size_t)STAGES * STAGE + 2 * STAGES * sizeof(uint64_t) +
-               (size_t)KS * rows * (D + 2) * sizeof(float) + 64;
+    // byte offset of (head hh, token t, dim d [multiple of 8]) inside a K or V
+    // region: D/64 column halves, each HG heads x 16 rows x 128 B, swizzled
+    __device__ __forceinline__ static uint32_t swz(int hh, int t, int d) {
+        return (uint32_t)((d >> 6) * (HG * HALF_BOX) + hh * HALF_BOX + t * 128 +
+                          ((((d & 63) >> 3) ^ (t & 7)) << 4));
+    }
+    __host__ __device__ static size_t merge_bytes(int rows) {
+        return KS > 1 ? (size_t)KS * HG * rows * (D + 2) * sizeof(float) : 0;
+    }
+    static int stages_for(int rows) {
+        const size_t fixed = 1024 + merge_bytes(rows) + 64;
+        const size_t avail = kSmemBudget > fixed ? kSmemBudget - fixed : 0;
+        int s = (int)(avail / (STAGE + 2 * sizeof(uint64_t)));
+        return s > 32 ? 32 : s;
+    }
+    static size_t smem_bytes(int rows, int stages) {
+        return 1024 + (size_t)stages * STAGE + 2 * stages * sizeof(uint64_t) + merge_bytes(rows) +
+               64;
     }
 };
 
-template <int D, int MT, int KS, int STAGES, typename QT>
-__global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
+template <int D, int MT, int HG, typename QT>
+__global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
     paged_attn_mma_kernel(const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv, const MmaParams p) {
-    using C = MmaCfg<D, MT, KS, STAGES>;
+    using C = MmaCfg<D, MT, HG>;
+    constexpr int KS = C::KS;
     extern __shared__ unsigned char smem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>(
+    unsigned char* ring = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char* ring = smem;
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(ring + STAGES * C::STAGE);
+    const int STAGES = p.stages;
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(ring + (size_t)STAGES * C::STAGE);
     uint64_t* empty_bar = full_bar + STAGES;
     float* merge = reinterpret_cast<float*>(empty_bar + STAGES);
-    int* s_flags = reinterpret_cast<int*>(merge + KS * p.rows * (D + 2));
+    int* s_flags = reinterpret_cast<int*>(reinterpret_cast<unsigned char*>(merge) +
+                                          C::merge_bytes(p.rows));
     volatile int* s_abort = s_flags;
     int* s_last = s_flags + 1;
 
@@ -217,7 +239,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
     const int B = p.batch, Hq = p.hq, G = p.group;
 
     // The plan must come from paged_plan_kernel for this batch shape.
-    if (p.plan[3] != kPlanMagic || p.plan[4] != B || p.plan[5] != p.hk) {
+    if (p.plan[3] != kPlanMagic || p.plan[4] != B || p.plan[5] != p.n_groups) {
         if (tid == 0 && blockIdx.x == 0) raise_flag(CX_DEV_BAD_QLEN);
         return;
     }
@@ -237,7 +259,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], MT);
+            mbar_init(&empty_bar[s], HG * MT);
         }
         s_flags[0] = 0;
         s_flags[1] = 0;
@@ -255,6 +277,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
         bool aborted = false;
         while (cur.next(seg)) {
             const int32_t* bt = p.tables + (int64_t)seg.b * p.table_stride;
+            const int zh = seg.g * HG;
             for (int k0 = 0; k0 < seg.cnt; k0 += 32) {
                 const int n = min(32, seg.cnt - k0);
                 int bid = -1;
@@ -277,13 +300,14 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
                             raise_flag(CX_DEV_WAIT_TIMEOUT);
                         } else if (bk >= 0) {
                             mbar_arrive_expect_tx(&full_bar[s], C::STAGE);
-                            const int z = (p.layer * p.n_blocks + bk) * p.hk + seg.h;
-                            unsigned char* kd = ring + s * C::STAGE;
+                            const int z = (p.layer * p.n_blocks + bk) * p.hk + zh;
+                            unsigned char* kd = ring + (size_t)s * C::STAGE;
 #pragma unroll
-                            for (int bx = 0; bx < D / 64; ++bx) {
-                                tma_load_3d(kd + bx * (kBlockTok * 128), &tmk, &full_bar[s], bx * 64, 0, z);
-                                tma_load_3d(kd + C::TILE + bx * (kBlockTok * 128), &tmv, &full_bar[s],
-                                            bx * 64, 0, z);
+                            for (int half = 0; half < D / 64; ++half) {
+                                tma_load_3d(kd + half * (HG * C::HALF_BOX), &tmk, &full_bar[s],
+                                            half * 64, 0, z);
+                                tma_load_3d(kd + C::TILES + half * (HG * C::HALF_BOX), &tmv,
+                                            &full_bar[s], half * 64, 0, z);
                             }
                         } else {
                             mbar_arrive(&full_bar[s]);  // bad id: release the slot, data unused
@@ -309,7 +333,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
     }
 
     // ------------------------------- consumers -------------------------------
-    const int mt = warp / KS, ks = warp % KS;
+    const int hh = warp % HG, mt = (warp / HG) % MT, ks = warp / (HG * MT);
     const int NCT = C::NCW * 32;
     const int ctid = tid;  // consumer threads are 0..NCT-1
     // per-lane ldmatrix coordinates
@@ -318,10 +342,11 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
     const int qr0 = lane >> 2, qc = 2 * (lane & 3);
     const int R0 = mt * 16 + qr0, R1 = R0 + 8;  // packed rows this lane owns
     const QT* qbase = static_cast<const QT*>(p.q);
+    const size_t slot_floats = (size_t)HG * p.rows * (D + 2);
 
     int ibase = 0;
     while (cur.next(seg)) {
-        const int b = seg.b, h = seg.h;
+        const int b = seg.b, h = seg.g * HG + hh;
         const int ctx = min(p.ctx_lens[b], (int)(p.table_stride * kBlockTok));
         const int sq = p.q_start ? p.q_start[b + 1] - p.q_start[b] : 1;
         const int64_t qs = p.q_start ? p.q_start[b] : b;
@@ -370,14 +395,14 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
                     raise_flag(CX_DEV_WAIT_TIMEOUT);
                 }
             } else {
-                const uint32_t kb = smem_addr(ring + s * C::STAGE);
-                const uint32_t vb = kb + C::TILE;
+                const uint32_t kb = smem_addr(ring + (size_t)s * C::STAGE);
+                const uint32_t vb = kb + C::TILES;
                 float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
                 float sb[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
                 for (int kk = 0; kk < C::KSTEP; ++kk) {
                     uint32_t f[4];
-                    ldmatrix_x4(f, kb + swz<D>(k_tok, kk * 16 + k_dsub));
+                    ldmatrix_x4(f, kb + C::swz(hh, k_tok, kk * 16 + k_dsub));
                     if (kk & 1) {
                         mma_bf16_16816(sb[0], qa[kk], f[0], f[1]);
                         mma_bf16_16816(sb[1], qa[kk], f[2], f[3]);
@@ -391,8 +416,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
                 for (int n = 0; n < 2; ++n)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) x[n][e] = (sa[n][e] + sb[n][e]) * p.scale_log2;
-                const int j = seg.j0 + k;
-                const int t0 = j * kBlockTok;
+                const int t0 = (seg.j0 + k) * kBlockTok;
                 const bool edge = (t0 + kBlockTok - 1 > pos0) ||
                                   (p.window > 0 && t0 <= ctx - 1 - p.window);
                 if (edge) {
@@ -443,7 +467,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
 #pragma unroll
                 for (int np = 0; np < C::KSTEP; ++np) {
                     uint32_t f[4];
-                    ldmatrix_x4_trans(f, vb + swz<D>(v_tok, np * 16 + v_dsub));
+                    ldmatrix_x4_trans(f, vb + C::swz(hh, v_tok, np * 16 + v_dsub));
                     mma_bf16_16816(o[2 * np], pa, f[0], f[1]);
                     mma_bf16_16816(o[2 * np + 1], pa, f[2], f[3]);
                 }
@@ -453,65 +477,91 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
         }
         ibase += seg.cnt;
 
-        // ---- merge the KS key slices of this (sequence, head) range ----
+        // ---- finish this (sequence, head group) range ----
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
         l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
         l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
         l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-        {
-            float* mrow = merge + (size_t)ks * p.rows * (D + 2);
-            if (R0 < rows_b) {
-                float* r = mrow + (size_t)R0 * (D + 2);
+        const int bg = b * p.n_groups + seg.g;
+        float* slot = p.partials + (size_t)(blockIdx.x + bg) * slot_floats;
+        if (KS == 1) {
+            // each warp owns complete rows: write straight from registers
 #pragma unroll
-                for (int n = 0; n < C::NT; ++n) {
-                    r[n * 8 + qc] = o[n][0];
-                    r[n * 8 + qc + 1] = o[n][1];
-                }
-                if ((lane & 3) == 0) {
-                    r[D] = m0;
-                    r[D + 1] = l0;
+            for (int half = 0; half < 2; ++half) {
+                const int R = half ? R1 : R0;
+                if (R >= rows_b) continue;
+                const float mm = half ? m1 : m0, ll = half ? l1 : l0;
+                if (seg.whole) {
+                    const float inv = ll > 0.f ? 1.f / ll : 0.f;
+                    const int64_t orow = (qs + R / G) * Hq + (int64_t)h * G + R % G;
+                    float* dst = p.out + orow * D;
+#pragma unroll
+                    for (int n = 0; n < C::NT; ++n) {
+                        *reinterpret_cast<float2*>(dst + n * 8 + qc) =
+                            make_float2(o[n][2 * half] * inv, o[n][2 * half + 1] * inv);
+                    }
+                } else {
+                    float* r = slot + ((size_t)hh * p.rows + R) * (D + 2);
+#pragma unroll
+                    for (int n = 0; n < C::NT; ++n)
+                        *reinterpret_cast<float2*>(r + n * 8 + qc) =
+                            make_float2(o[n][2 * half], o[n][2 * half + 1]);
+                    if ((lane & 3) == 0) {
+                        r[D] = mm;
+                        r[D + 1] = ll;
+                    }
                 }
             }
-            if (R1 < rows_b) {
-                float* r = mrow + (size_t)R1 * (D + 2);
+        } else {
+            // merge the KS key slices through shared memory
+            {
+                float* mrow = merge + ((size_t)ks * HG + hh) * p.rows * (D + 2);
 #pragma unroll
-                for (int n = 0; n < C::NT; ++n) {
-                    r[n * 8 + qc] = o[n][2];
-                    r[n * 8 + qc + 1] = o[n][3];
-                }
-                if ((lane & 3) == 0) {
-                    r[D] = m1;
-                    r[D + 1] = l1;
-                }
-            }
-        }
-        named_bar_sync(1, NCT);
-        const int bh = b * p.hk + h;
-        float* slot = p.partials + (size_t)(blockIdx.x + bh) * p.rows * (D + 2);
-        for (int e = ctid; e < rows_b * D; e += NCT) {
-            const int R = e / D, d = e - R * D;
-            float M = -INFINITY;
+                for (int half = 0; half < 2; ++half) {
+                    const int R = half ? R1 : R0;
+                    if (R >= rows_b) continue;
+                    float* r = mrow + (size_t)R * (D + 2);
 #pragma unroll
-            for (int s2 = 0; s2 < KS; ++s2)
-                M = fmaxf(M, merge[((size_t)s2 * p.rows + R) * (D + 2) + D]);
-            float L = 0.f, O = 0.f;
-            if (M != -INFINITY) {
-#pragma unroll
-                for (int s2 = 0; s2 < KS; ++s2) {
-                    const float* r = merge + ((size_t)s2 * p.rows + R) * (D + 2);
-                    const float wgt = exp2f(r[D] - M);
-                    L += r[D + 1] * wgt;
-                    O += r[d] * wgt;
+                    for (int n = 0; n < C::NT; ++n) {
+                        r[n * 8 + qc] = o[n][2 * half];
+                        r[n * 8 + qc + 1] = o[n][2 * half + 1];
+                    }
+                    if ((lane & 3) == 0) {
+                        r[D] = half ? m1 : m0;
+                        r[D + 1] = half ? l1 : l0;
+                    }
                 }
             }
-            if (seg.whole) {
-                const int64_t orow = (qs + R / G) * Hq + (int64_t)h * G + R % G;
-                p.out[orow * D + d] = L > 0.f ? O / L : 0.f;
-            } else {
-                slot[(size_t)R * (D + 2) + d] = O;
-                if (d == 0) {
-                    slot[(size_t)R * (D + 2) + D] = M;
-                    slot[(size_t)R * (D + 2) + D + 1] = L;
+            named_bar_sync(1, NCT);
+            for (int e = ctid; e < HG * rows_b * D; e += NCT) {
+                const int d = e % D;
+                const int R = (e / D) % rows_b;
+                const int eh = e / (D * rows_b);
+                float M = -INFINITY;
+#pragma unroll
+                for (int s2 = 0; s2 < KS; ++s2)
+                    M = fmaxf(M, merge[(((size_t)s2 * HG + eh) * p.rows + R) * (D + 2) + D]);
+                float L = 0.f, O = 0.f;
+                if (M != -INFINITY) {
+#pragma unroll
+                    for (int s2 = 0; s2 < KS; ++s2) {
+                        const float* r = merge + (((size_t)s2 * HG + eh) * p.rows + R) * (D + 2);
+                        const float wgt = exp2f(r[D] - M);
+                        L += r[D + 1] * wgt;
+                        O += r[d] * wgt;
+                    }
+                }
+                if (seg.whole) {
+                    const int64_t orow =
+                        (qs + R / G) * Hq + (int64_t)(seg.g * HG + eh) * G + R % G;
+                    p.out[orow * D + d] = L > 0.f ? O / L : 0.f;
+                } else {
+                    float* r = slot + ((size_t)eh * p.rows + R) * (D + 2);
+                    r[d] = O;
+                    if (d == 0) {
+                        r[D] = M;
+                        r[D + 1] = L;
+                    }
                 }
             }
         }
@@ -519,9 +569,9 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
             __threadfence();
             named_bar_sync(1, NCT);
             if (ctid == 0) {
-                const int first_u = p.seq_start[b] + h * seg.nb;
+                const int first_u = p.seq_start[b] + seg.g * seg.nb;
                 const int pf = first_u / chunk, pl = (first_u + seg.nb - 1) / chunk;
-                const int prev = atomicAdd(&p.counters[bh], 1);
+                const int prev = atomicAdd(&p.counters[bg], 1);
                 *s_last = (prev == pl - pf) ? (pf | (pl << 16)) + 1 : 0;
             }
             named_bar_sync(1, NCT);
@@ -529,28 +579,27 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, KS, STAGES>::THREADS, 1)
             if (last) {
                 __threadfence();
                 const int pf = (last - 1) & 0xffff, pl = (last - 1) >> 16;
-                for (int e = ctid; e < rows_b * D; e += NCT) {
-                    const int R = e / D, d = e - R * D;
+                for (int e = ctid; e < HG * rows_b * D; e += NCT) {
+                    const int d = e % D;
+                    const int R = (e / D) % rows_b;
+                    const int eh = e / (D * rows_b);
+                    const size_t roff = ((size_t)eh * p.rows + R) * (D + 2);
                     float M = -INFINITY;
-                    for (int pp = pf; pp <= pl; ++pp) {
-                        const float* r = p.partials + (size_t)(pp + bh) * p.rows * (D + 2) +
-                                         (size_t)R * (D + 2);
-                        M = fmaxf(M, __ldcg(r + D));
-                    }
+                    for (int pp = pf; pp <= pl; ++pp)
+                        M = fmaxf(M, __ldcg(p.partials + (size_t)(pp + bg) * slot_floats + roff + D));
                     float L = 0.f, O = 0.f;
                     if (M != -INFINITY) {
                         for (int pp = pf; pp <= pl; ++pp) {
-                            const float* r = p.partials + (size_t)(pp + bh) * p.rows * (D + 2) +
-                                             (size_t)R * (D + 2);
+                            const float* r = p.partials + (size_t)(pp + bg) * slot_floats + roff;
                             const float wgt = exp2f(__ldcg(r + D) - M);
                             L += __ldcg(r + D + 1) * wgt;
                             O += __ldcg(r + d) * wgt;
                         }
                     }
-                    const int64_t orow = (qs + R / G) * Hq + (int64_t)h * G + R % G;
+                    const int64_t orow = (qs + R / G) * Hq + (int64_t)(seg.g * HG + eh) * G + R % G;
                     p.out[orow * D + d] = L > 0.f ? O / L : 0.f;
                 }
-                if (ctid == 0) p.counters[bh] = 0;
+                if (ctid == 0) p.counters[bg] = 0;
             }
         }
         named_bar_sync(1, NCT);
@@ -575,15 +624,15 @@ static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
 }
 
 // 3-D view of a bf16 pool: (head_dim, 16 slots, layers*blocks*heads tiles),
-// box 64 x 16 x 1 with 128-byte swizzle.
-static int make_pool_tmap(CUtensorMap* m, void* base, const cx_pool* p) {
+// box 64 x 16 x hg (hg consecutive heads of one block) with 128-byte swizzle.
+static int make_pool_tmap(CUtensorMap* m, void* base, const cx_pool* p, int hg) {
     auto enc = tmap_encoder();
     if (!enc) return fail(CX_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t dims[3] = {(cuuint64_t)p->head_dim, (cuuint64_t)p->block_size,
                                 (cuuint64_t)(p->n_layers * p->n_blocks * p->n_kv_heads)};
     const cuuint64_t strides[2] = {(cuuint64_t)p->head_dim * 2,
                                    (cuuint64_t)(p->block_size * p->head_dim * 2)};
-    const cuuint32_t box[3] = {64, (cuuint32_t)p->block_size, 1};
+    const cuuint32_t box[3] = {64, (cuuint32_t)p->block_size, (cuuint32_t)hg};
     const cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -592,49 +641,65 @@ static int make_pool_tmap(CUtensorMap* m, void* base, const cx_pool* p) {
     return CX_OK;
 }
 
-constexpr int kStages = 16;
+struct MmaShape {
+    int mt, hg, ks, n_groups;
+};
+
+// Heads per unit: as many as keep <= 8 consumer warps (8 / m-tiles), a power
+// of two dividing the KV head count.
+static MmaShape mma_shape(int64_t hk, int64_t rows) {
+    MmaShape s{};
+    s.mt = (int)((rows + 15) / 16);
+    const int cap = s.mt == 1 ? 8 : (s.mt == 2 ? 4 : 2);
+    s.hg = 1;
+    while (s.hg * 2 <= cap && hk % (s.hg * 2) == 0) s.hg *= 2;
+    s.ks = s.hg * s.mt >= kConsumerWarps ? 1 : kConsumerWarps / (s.hg * s.mt);
+    s.n_groups = (int)(hk / s.hg);
+    return s;
+}
 
 struct WsLayout {
     size_t plan, seq, lo, cnt, part, total;
 };
 
-static int mt_for_rows(int64_t rows) { return (int)((rows + 15) / 16); }
-static int ks_for_mt(int mt) { return mt == 1 ? 8 : (mt == 2 ? 4 : 2); }
-
 static WsLayout ws_layout(int64_t batch, int64_t hk, int64_t rows, int64_t d, int64_t grid) {
+    const MmaShape sh = mma_shape(hk, rows);
     auto up = [](size_t x, size_t a) { return (x + a - 1) / a * a; };
     WsLayout w{};
     w.plan = 0;
     w.seq = 64;
     w.lo = up(w.seq + (batch + 1) * 4, 16);
     w.cnt = up(w.lo + batch * 4, 16);
-    w.part = up(w.cnt + batch * hk * 4, 256);
-    w.total = w.part + (size_t)(grid + batch * hk) * rows * (d + 2) * 4;
+    w.part = up(w.cnt + batch * sh.n_groups * 4, 256);
+    w.total = w.part + (size_t)(grid + batch * sh.n_groups) * sh.hg * rows * (d + 2) * 4;
     return w;
 }
 
-template <int D, int MT, typename QT>
-static int launch_mma_cfg(const CUtensorMap& tk, const CUtensorMap& tv, const MmaParams& p,
+template <int D, int MT, int HG, typename QT>
+static int launch_mma_cfg(const CUtensorMap& tk, const CUtensorMap& tv, MmaParams p,
                           cudaStream_t st, int grid) {
-    constexpr int KS = MT == 1 ? 8 : (MT == 2 ? 4 : 2);
-    using C = MmaCfg<D, MT, KS, kStages>;
-    auto kern = paged_attn_mma_kernel<D, MT, KS, kStages, QT>;
-    const size_t smem = C::smem_bytes(p.rows);
+    using C = MmaCfg<D, MT, HG>;
+    auto kern = paged_attn_mma_kernel<D, MT, HG, QT>;
+    p.stages = C::stages_for(p.rows);
+    p.stage_bytes = C::STAGE;
+    if (p.stages < 2) return fail(CX_ERR_UNSUPPORTED, "paged attention: shared memory too small");
+    const size_t smem = C::smem_bytes(p.rows, p.stages);
     CX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     kern<<<grid, C::THREADS, smem, st>>>(tk, tv, p);
     return check_launch("paged_attn_mma_kernel");
 }
 
 template <int D, typename QT>
-static int launch_mma_d(int mt, const CUtensorMap& tk, const CUtensorMap& tv, const MmaParams& p,
-                        cudaStream_t st, int grid) {
-    switch (mt) {
-        case 1: return launch_mma_cfg<D, 1, QT>(tk, tv, p, st, grid);
-        case 2: return launch_mma_cfg<D, 2, QT>(tk, tv, p, st, grid);
-        case 3: return launch_mma_cfg<D, 3, QT>(tk, tv, p, st, grid);
-        case 4: return launch_mma_cfg<D, 4, QT>(tk, tv, p, st, grid);
-        default: return fail(CX_ERR_UNSUPPORTED, "paged attention: more than 64 packed rows");
-    }
+static int launch_mma_d(const MmaShape& sh, const CUtensorMap& tk, const CUtensorMap& tv,
+                        const MmaParams& p, cudaStream_t st, int grid) {
+#define CX_CASE(MT_, HG_) \
+    if (sh.mt == MT_ && sh.hg == HG_) return launch_mma_cfg<D, MT_, HG_, QT>(tk, tv, p, st, grid);
+    CX_CASE(1, 8) CX_CASE(1, 4) CX_CASE(1, 2) CX_CASE(1, 1)
+    CX_CASE(2, 4) CX_CASE(2, 2) CX_CASE(2, 1)
+    CX_CASE(3, 2) CX_CASE(3, 1)
+    CX_CASE(4, 2) CX_CASE(4, 1)
+#undef CX_CASE
+    return fail(CX_ERR_UNSUPPORTED, "paged attention: no kernel for this row/head shape");
 }
 
 static bool mma_eligible(const cx_pool* pool, const cx_attn_batch* b, int32_t q_dtype) {
@@ -701,6 +766,7 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
 
     const int64_t G = b.n_q_heads / pool->n_kv_heads;
     const int64_t rows = G * max_q;
+    const MmaShape sh = mma_shape(pool->n_kv_heads, rows);
     const int grid = grid_size();
     const WsLayout wl = ws_layout(b.batch, pool->n_kv_heads, rows, pool->head_dim, grid);
     if (!ws || ws_bytes < wl.total)
@@ -722,6 +788,8 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
     p.group = (int)G;
     p.max_q = (int)max_q;
     p.rows = (int)rows;
+    p.hg = sh.hg;
+    p.n_groups = sh.n_groups;
     p.n_blocks = (int)pool->n_blocks;
     p.layer = (int)layer;
     p.window = b.window > 0 ? (int)b.window : 0;
@@ -740,16 +808,15 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
         if (rc) return rc;
     }
     CUtensorMap tk, tv;
-    rc = make_pool_tmap(&tk, pool->k, pool);
+    rc = make_pool_tmap(&tk, pool->k, pool, sh.hg);
     if (rc) return rc;
-    rc = make_pool_tmap(&tv, pool->v, pool);
+    rc = make_pool_tmap(&tv, pool->v, pool, sh.hg);
     if (rc) return rc;
-    const int mt = mt_for_rows(rows);
     if (pool->head_dim == 128)
-        return q_dtype == CX_F32 ? launch_mma_d<128, float>(mt, tk, tv, p, st, grid)
-                                 : launch_mma_d<128, __nv_bfloat16>(mt, tk, tv, p, st, grid);
-    return q_dtype == CX_F32 ? launch_mma_d<64, float>(mt, tk, tv, p, st, grid)
-                             : launch_mma_d<64, __nv_bfloat16>(mt, tk, tv, p, st, grid);
+        return q_dtype == CX_F32 ? launch_mma_d<128, float>(sh, tk, tv, p, st, grid)
+                                 : launch_mma_d<128, __nv_bfloat16>(sh, tk, tv, p, st, grid);
+    return q_dtype == CX_F32 ? launch_mma_d<64, float>(sh, tk, tv, p, st, grid)
+                             : launch_mma_d<64, __nv_bfloat16>(sh, tk, tv, p, st, grid);
 }
 
 }  // namespace cx
