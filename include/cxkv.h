@@ -151,6 +151,27 @@ int cx_paged_verify(const cx_pool* pool, int64_t layer, const cx_attn_batch* bat
                     void* workspace, size_t workspace_bytes, int32_t replan,
                     void* stream);
 
+/* Paged decode that allocates nothing — no counterpart in the reference (its
+ * NumPy path needs no device memory at all).  Same inputs, outputs and
+ * results as cx_paged_decode, but the plan / split-K partials / merge tickets
+ * live in a scratch array compiled into this library (8 MiB per device,
+ * resident on every GPU that loads the library until the process exits), for
+ * callers that cannot allocate device memory: a serving process whose HBM is
+ * already fully reserved by the block pool and its own allocator, or a host
+ * runtime behind a plain C FFI with no device allocator to give us.
+ * - Rejects, with CX_ERR_WORKSPACE and a message, any batch whose scratch
+ *   need (cx_paged_workspace_bytes) exceeds 8 MiB; it never calls cudaMalloc,
+ *   cudaFree or any allocating library routine.
+ * - The first call on a device resolves the scratch address with
+ *   cudaGetSymbolAddress (that device must be current); make that first call
+ *   before any stream capture.
+ * - Every call re-plans and zeroes the merge tickets itself.  All calls on a
+ *   device share the one scratch array, which keeps the last call's contents:
+ *   calls that overlap on the GPU (different streams, no ordering between
+ *   them) race on it and must be serialised by the caller. */
+int cx_paged_decode_static(const cx_pool* pool, int64_t layer, const cx_attn_batch* batch,
+                           const void* q, int32_t q_dtype, float* out, void* stream);
+
 /* Dense attention — replaces flash_attention / naive_attention on contiguous
  * arrays (chenxing/core/attention.py:43-148): q [b][hq][sq][d],
  * k [b][hk][sk][d], v [b][hk][sk][dv] (kv_dtype), out float32 [b][hq][sq][dv].
