@@ -362,22 +362,25 @@ def run_ours(args):
         if sampler:
             sampler.start()
             time.sleep(0.5)
-        evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(layers)]
-               for _ in range(args.steps)]
+        # per-launch decode timing on the last two timed steps (event records
+        # between launches cost ~1 us each, so not on every step)
+        ev_steps = set(range(max(0, args.steps - 2), args.steps))
+        evs = {i: [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(layers)]
+               for i in ev_steps}
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         launches[0] = 0
         barrier()
         torch.cuda.synchronize(dev)
         start.record(stream)
         for i in range(args.steps):
-            one_step(args.warmup + i, evs[i])
+            one_step(args.warmup + i, evs.get(i))
         end.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
         clocks = sampler.stop() if sampler else None
         timed_launches = launches[0]
     ms = start.elapsed_time(end)
-    dec_ms = [e[0].elapsed_time(e[1]) for step in evs for e in step]
+    dec_ms = [e[0].elapsed_time(e[1]) for step in evs.values() for e in step]
     flags = _lib.device_flags(clear=True, device=dev)
     if flags:
         raise RuntimeError(f"device flags during timing: {_lib.describe_flags(flags)}")
@@ -393,8 +396,9 @@ def run_ours(args):
 
     # roofline of the dominant kernel (paged decode), per launch
     avg_dec_ms = float(np.mean(dec_ms))
-    kv_tok_layer = units / (args.steps * layers)        # keys per decode launch
-    nblk = sum(-(-int(c) // BS) for c in ctx0) + BATCH * (args.warmup + args.steps / 2) / BS
+    ev_units = [units_step[args.warmup + i] for i in sorted(ev_steps)]
+    kv_tok_layer = float(np.mean(ev_units)) / layers       # keys per timed decode launch
+    nblk = sum(-(-int(c) // BS) for c in ctx0) + BATCH * (args.warmup + args.steps) / BS
     alg_bytes = kv_tok_layer * UNIT_BYTES + BATCH * HQ * D * (ELEM + 4) + 4 * nblk
     achieved = alg_bytes / (avg_dec_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
@@ -403,7 +407,8 @@ def run_ours(args):
                 "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
                 "traffic": (tpu * kv_tok_layer) if tpu else None,
                 "algorithmic_bytes_per_launch": alg_bytes, "avg_launch_ms": avg_dec_ms,
-                "decode_share_of_step": sum(dec_ms) / ms}
+                "timed_launches": len(dec_ms),
+                "decode_share_of_step": sum(dec_ms) / (ms * len(ev_steps) / args.steps)}
     step_gbs = (units * UNIT_BYTES) / (ms / 1e3) / 1e9
 
     # end to end: inputs from pinned host memory and outputs back, every step

@@ -209,7 +209,12 @@ struct MmaCfg {
         const size_t fixed = 1024 + merge_bytes(rows) + 64;
         const size_t avail = kSmemBudget > fixed ? kSmemBudget - fixed : 0;
         int s = (int)(avail / (STAGE + 2 * sizeof(uint64_t)));
-        return s > 32 ? 32 : s;
+        s = s > 32 ? 32 : s;
+        // The KS consumer warps of one (head, row tile) share each stage;
+        // mbarrier parity is derived from (iteration / STAGES), so a ring
+        // whose length is not a multiple of KS would let two consumers wait
+        // on the same barrier phase for different fills.
+        return (s / KS) * KS;
     }
     static size_t smem_bytes(int rows, int stages) {
         return 1024 + (size_t)stages * STAGE + 2 * stages * sizeof(uint64_t) + merge_bytes(rows) +
@@ -237,6 +242,10 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int B = p.batch, Hq = p.hq, G = p.group;
+    if (STAGES < 2 || STAGES % KS != 0) {
+        if (tid == 0 && blockIdx.x == 0) raise_flag(CX_DEV_BAD_QLEN);
+        return;
+    }
 
     // The plan must come from paged_plan_kernel for this batch shape.
     if (p.plan[3] != kPlanMagic || p.plan[4] != B || p.plan[5] != p.n_groups) {
@@ -682,7 +691,8 @@ static int launch_mma_cfg(const CUtensorMap& tk, const CUtensorMap& tv, MmaParam
     auto kern = paged_attn_mma_kernel<D, MT, HG, QT>;
     p.stages = C::stages_for(p.rows);
     p.stage_bytes = C::STAGE;
-    if (p.stages < 2) return fail(CX_ERR_UNSUPPORTED, "paged attention: shared memory too small");
+    if (p.stages < 2 || p.stages % C::KS != 0)
+        return fail(CX_ERR_UNSUPPORTED, "paged attention: shared memory too small");
     const size_t smem = C::smem_bytes(p.rows, p.stages);
     CX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     kern<<<grid, C::THREADS, smem, st>>>(tk, tv, p);
