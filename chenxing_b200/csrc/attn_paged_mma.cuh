@@ -16,7 +16,7 @@
 // workspace (log-sum-exp merge) and writes the final rows.
 //
 // Inside a CTA: the last warp is the producer.  Its lanes fetch 32 block ids
-// of the table at a time; lane 0 issues the TMA loads (no multicast) of each
+// of the table at a time; lane 0 issues the TMA loads (CTA-local destination) of each
 // unit into a ring of shared-memory stages, completing on per-stage
 // mbarriers.  Consumer warps are indexed (hh, mt, ks): head hh of the group,
 // 16 packed query rows mt (row = query token * G + head-in-group), and key

@@ -127,7 +127,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
-// 3-D tiled TMA load (no multicast) into CTA shared memory, completing on `bar`.
+// 3-D tiled TMA load into this CTA's own shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_t* bar, int x,
                                             int y, int z) {
     asm volatile(
