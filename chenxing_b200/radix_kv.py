@@ -9,7 +9,8 @@ libcxkv kernel:
 
 * ``write_layer``  -> ``cx_kv_append``  (slot-mapped scatter, radix_kv.py:113-128)
 * ``read_layer``   -> ``cx_kv_gather``  (radix_kv.py:130-144)
-* ``copy_blocks`` / ``cow_tail`` -> ``cx_block_copy`` (no reference counterpart)
+* ``copy_blocks`` / ``cow_tail`` / ``compact`` -> ``cx_block_copy`` (no reference
+  counterpart)
 * ``append_batch`` / ``decode_batch`` / ``verify_batch`` — batched forms over
   many sequences (see ``chenxing_b200.batch``).
 
@@ -201,6 +202,45 @@ class RadixIndex:
                     best = c
         return best
 
+    def plan_compaction(self, tables=(), max_moves: int | None = None) -> tuple[list, list]:
+        """Relabel in-use blocks so they pack into the lowest ids.
+
+        No reference counterpart (the reference never moves data).  In use =
+        not on the free list, so blocks the reference leaks (finished
+        sequences' private blocks) are moved like any other.  With
+        ``n_used = n_blocks - free_blocks``, every in-use id >= n_used is
+        paired, highest first, with a free id < n_used, lowest first; at most
+        ``max_moves`` pairs.  Radix-node block lists and every table in
+        ``tables`` (lists of ids, edited in place) are rewritten; the free
+        list keeps its surviving ids in FIFO order and then takes the vacated
+        ids in ascending order.  Returns (src, dst) for the data copy, which
+        the caller must issue before any further write to a dst block.
+        Every live block table must be passed, or it keeps stale ids.
+        """
+        n_used = self.n_blocks - len(self._free)
+        holes = [b for b in range(n_used) if b in self._free]
+        high = [b for b in range(self.n_blocks - 1, n_used - 1, -1) if b not in self._free]
+        n = min(len(holes), len(high))
+        if max_moves is not None:
+            n = min(n, max(0, int(max_moves)))
+        src, dst = high[:n], holes[:n]
+        if not n:
+            return [], []
+        remap = dict(zip(src, dst))
+        stack = [self._root]
+        while stack:
+            node = stack.pop()
+            if node.blocks:
+                node.blocks[:] = [remap.get(b, b) for b in node.blocks]
+            stack.extend(node.children.values())
+        for t in tables:
+            t[:] = [remap.get(b, b) for b in t]
+        for d in dst:
+            del self._free[d]
+        for s in sorted(src):
+            self._free[s] = None
+        return src, dst
+
     def stats(self) -> dict:
         total, stack = 0, [self._root]
         while stack:
@@ -351,6 +391,16 @@ class RadixPagedKVCache(RadixIndex):
         _lib.check(_lib.lib().cx_block_copy(self._pool, s.data_ptr(), t.data_ptr(), len(src),
                                             n_slots, _lib.stream_ptr(self.device)),
                    "cx_block_copy")
+
+    def compact(self, tables=(), max_moves: int | None = None) -> int:
+        """Pack in-use blocks into the lowest ids (``plan_compaction``) and move
+        their K/V, every layer, with one ``cx_block_copy``; returns the number
+        of blocks moved.  Runs on the cache's current stream, so later kernels
+        on that stream see the moved data."""
+        src, dst = self.plan_compaction(tables, max_moves)
+        if src:
+            self.copy_blocks(src, dst)
+        return len(src)
 
     def cow_tail(self, block_table: list, n_tokens: int, is_shared) -> tuple | None:
         """Copy-on-write of a shared, partially filled tail block.

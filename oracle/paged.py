@@ -18,6 +18,11 @@ Restates how the reference drives the KV hot path, one sequence at a time:
   reference has no CoW (it shares whole blocks only, ``radix_kv.py:16-21``);
   this oracle defines it by construction: take ``alloc_block()``, copy the
   ``r = n_tokens % bs`` valid slots of every layer, swap the table entry.
+* ``compact``         — block-pool compaction after eviction; also absent from
+  the reference (it never moves data).  Defined by construction: two
+  pointers, the lowest free id below ``n_used`` and the highest in-use id at
+  or above it, are paired until they cross; data copied, radix nodes and
+  tables relabelled, vacated ids appended to the free list in ascending order.
 """
 from __future__ import annotations
 
@@ -25,7 +30,7 @@ import numpy as np
 
 from .attention import CausalMask, flash_attention, naive_attention
 
-__all__ = ["slot_mapping", "ensure_capacity", "rollback", "cow_tail",
+__all__ = ["slot_mapping", "ensure_capacity", "rollback", "cow_tail", "compact",
            "attend_sequence", "paged_attention_batch"]
 
 
@@ -67,6 +72,43 @@ def cow_tail(cache, block_table, n_tokens, is_shared):
     cache.v_pool[:, dst, :r] = cache.v_pool[:, src, :r]
     block_table[j] = dst
     return src, dst, r
+
+
+def compact(cache, tables, max_moves=None):
+    """Pack in-use blocks into the lowest ids; returns the (src, dst) moves."""
+    free = cache._free
+    n_used = cache.n_blocks - len(free)
+    lo, hi, moves = 0, cache.n_blocks - 1, []
+    while max_moves is None or len(moves) < max_moves:
+        while lo < n_used and lo not in free:
+            lo += 1
+        while hi >= n_used and hi in free:
+            hi -= 1
+        if lo >= n_used or hi < n_used:
+            break
+        moves.append((hi, lo))
+        lo, hi = lo + 1, hi - 1
+    if not moves:
+        return []
+    if hasattr(cache, "k_pool"):
+        for s, d in moves:
+            cache.k_pool[:, d] = cache.k_pool[:, s]
+            cache.v_pool[:, d] = cache.v_pool[:, s]
+    new_id = dict(moves)
+    todo = [cache._root]
+    while todo:
+        node = todo.pop()
+        node.blocks = [new_id.get(b, b) for b in node.blocks]
+        todo.extend(node.children.values())
+    for t in tables:
+        for i, b in enumerate(t):
+            if b in new_id:
+                t[i] = new_id[b]
+    for _, d in moves:
+        del free[d]
+    for s in sorted(s for s, _ in moves):
+        free[s] = None
+    return moves
 
 
 def attend_sequence(cache, block_table, n_past, layer, q, k_new, v_new,

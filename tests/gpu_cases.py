@@ -109,3 +109,44 @@ class PagedCase:
                     f"seq {b} ctx {self.ctx[b]}: max abs err {err} > {rtol} * {scale}"
                 worst = max(worst, err / bound if bound > 0 else 0.0)
         return worst
+
+
+def pool_rows(cache, layer, table, lo, hi):
+    """K, V of positions [lo, hi) of one sequence, read straight out of the
+    pool tensors with torch indexing (checker side, not the product path);
+    float32 NumPy arrays of shape (hi - lo, H, D)."""
+    bs = cache.block_size
+    pos = torch.arange(lo, hi, device=cache.device)
+    bt = torch.as_tensor(table, dtype=torch.int64, device=cache.device)[pos // bs]
+    k = cache._k[layer, bt, :, pos % bs]
+    v = cache._v[layer, bt, :, pos % bs]
+    return k.float().cpu().numpy(), v.float().cpu().numpy()
+
+
+def oracle_rows(q, k, v, window=None):
+    """Oracle attention of the last len(q) positions of a key run: q (T, hq, D),
+    k / v (S, hk, D) float32 -> (T, hq, D).  With a window the run may start
+    after position 0: the mask depends only on position differences."""
+    q4 = np.ascontiguousarray(q.transpose(1, 0, 2)[None])
+    k4 = np.ascontiguousarray(k.transpose(1, 0, 2)[None])
+    v4 = np.ascontiguousarray(v.transpose(1, 0, 2)[None])
+    if window is None:
+        o = flash_attention(q4, k4, v4, CausalMask())
+    else:
+        o = naive_attention(q4, k4, v4, CausalMask(window))
+    return o[0].transpose(1, 0, 2)
+
+
+def assert_close_rows(got, ref, rtol=BF16_RTOL, what=""):
+    assert np.isfinite(got).all(), f"non-finite output {what}"
+    err = float(np.abs(got - ref).max())
+    bound = rtol * float(np.abs(ref).max())
+    assert err <= bound, f"{what}: max abs err {err} > {bound}"
+    return err / bound if bound else 0.0
+
+
+def claim_blocks(index, ids):
+    """Take ``ids`` out of an index's FIFO free list (harness placement of
+    scattered tables); works on the product index and the oracle alike."""
+    for b in ids:
+        del index._free[int(b)]

@@ -133,3 +133,167 @@ def test_partition_by_context_is_balanced_and_complete():
     assert flat == list(range(1024))
     loads = [int(ctx[g].sum()) for g in groups]
     assert max(loads) - min(loads) <= int(ctx.max())
+
+
+def _churned_pair(seed):
+    """The product index and the oracle driven through the same random churn:
+    allocations into per-sequence tables, published prefixes, LRU evictions
+    and frees, leaving holes all over the id range."""
+    from oracle.radix_kv import OraclePagedKVCache
+    rng = np.random.default_rng(seed)
+    nb, bs = 300, 4
+    idx = RadixIndex(nb, bs, clock=logical_clock())
+    orc = OraclePagedKVCache(nb, bs, 1, 1, 1, with_pool=False, clock=logical_clock())
+    tabs, otabs = [], []
+    for step in range(40):
+        n = int(rng.integers(1, 9))
+        t, ot = [], []
+        grow_table(idx, t, n * bs)
+        from oracle.paged import ensure_capacity
+        ensure_capacity(orc, ot, n * bs)
+        assert t == ot
+        kind = rng.integers(0, 3)
+        if kind == 0 and n >= 2:              # publish whole blocks in the tree;
+            toks = [int(step * 1000 + i) for i in range((n - 1) * bs)]
+            idx.insert(toks, t[:n - 1])       # the tree owns them from now on
+            orc.insert(toks, ot[:n - 1])
+            t, ot = t[n - 1:], ot[n - 1:]
+        if kind == 1 and tabs:                # a sequence finishes and frees
+            j = int(rng.integers(0, len(tabs)))
+            for b in tabs.pop(j):
+                idx._free_block(b)
+            for b in otabs.pop(j):
+                orc._free_block(b)
+        if rng.random() < 0.3:
+            k = int(rng.integers(1, 6))
+            assert idx.evict(k) == orc.evict(k)
+        tabs.append(t)
+        otabs.append(ot)
+    return idx, orc, tabs, otabs
+
+
+@pytest.mark.parametrize("max_moves", [None, 0, 1, 7])
+def test_compaction_plan_matches_oracle(max_moves):
+    from oracle.paged import compact
+    from replay import tree_sig
+    for seed in range(3):
+        idx, orc, tabs, otabs = _churned_pair(seed)
+        n_used = idx.n_blocks - idx.free_blocks
+        src, dst = idx.plan_compaction(tabs, max_moves)
+        moves = compact(orc, otabs, max_moves)
+        assert list(zip(src, dst)) == moves
+        assert tabs == otabs
+        assert list(idx._free) == list(orc._free)
+        assert tree_sig(idx._root) == tree_sig(orc._root)
+        if max_moves is None:
+            live = {b for t in tabs for b in t}
+            assert all(b < n_used for b in live)
+            assert all(b >= n_used for b in idx._free)
+        # a second full pass after a full pass moves nothing
+        if max_moves is None:
+            assert idx.plan_compaction(tabs) == ([], [])
+
+
+@pytest.mark.parametrize("free_private,mode", [(False, "reference"), (True, "reference"),
+                                               (True, "suffix")])
+def test_batched_engine_metadata_matches_oracle_replay(free_private, mode):
+    """Continuous-batching churn through BatchedKVEngine's host half (bare
+    RadixIndex, no device): admissions with shared-prefix hits, batched
+    decode / verify steps, finishes that publish their prefix, LRU eviction
+    under pressure and compaction; every table, length, the free list and the
+    radix tree equal the oracle's per-sequence replay after every step."""
+    from chenxing_b200.engine import BatchedKVEngine
+    from engine_replay import OracleEngine
+    from oracle.radix_kv import OraclePagedKVCache
+    from replay import tree_sig
+    rng = np.random.default_rng(5)
+    nb, bs = 400, 4
+    idx = RadixIndex(nb, bs, clock=logical_clock())
+    orc = OraclePagedKVCache(nb, bs, 1, 1, 1, with_pool=False, clock=logical_clock())
+    eng = BatchedKVEngine(idx, n_q_heads=1, free_private_blocks=free_private,
+                          publish_mode=mode)
+    ref = OracleEngine(orc, free_private, suffix_publish=mode == "suffix")
+    prefixes = [[7000 + 100 * p + i for i in range(3 * bs)] for p in range(3)]
+    next_id = 0
+
+    def admit():
+        nonlocal next_id
+        n = int(rng.integers(1, 30))
+        toks = (prefixes[int(rng.integers(0, 3))] if rng.random() < 0.5 else []) + \
+            [int(x) for x in rng.integers(0, 500, size=n)]
+        eng.add(next_id, toks)
+        ref.add(next_id, toks)
+        q = len(toks) - eng.seqs[next_id].n_tokens
+        try:
+            p = eng.plan_host([next_id], [q])
+        except OutOfKVCacheError:
+            with pytest.raises(Exception):
+                ref.step([next_id], [q])
+            return
+        ref.step([next_id], [q])
+        eng.commit(p)
+        ref.commit([next_id], [q])
+        next_id += 1
+
+    def check():
+        assert {k: (s.block_table, s.n_tokens) for k, s in eng.seqs.items()} == \
+            {k: (s["table"], s["n"]) for k, s in ref.seqs.items()}
+        assert list(idx._free) == list(orc._free)
+        assert tree_sig(idx._root) == tree_sig(orc._root)
+
+    for _ in range(12):
+        admit()
+    check()
+    for step in range(25):
+        ids = sorted(eng.seqs)
+        q = [int(rng.integers(1, 6)) if step % 4 == 3 else 1 for _ in ids]
+        try:
+            p = eng.plan_host(ids, q)
+        except OutOfKVCacheError:
+            with pytest.raises(Exception):
+                ref.step(ids, q)
+            break
+        ref.step(ids, q)
+        eng.commit(p)
+        ref.commit(ids, q)
+        check()
+        for sid in ids:
+            if rng.random() < 0.15:
+                for t in range(int(rng.integers(1, 4))):
+                    eng.extend_tokens(sid, [int(rng.integers(0, 500))])
+                    ref.seqs[sid]["tokens"].append(eng.seqs[sid].tokens[-1])
+        for sid in list(eng.seqs):
+            if rng.random() < 0.1:
+                eng.finish(sid)
+                ref.finish(sid)
+        for _ in range(int(rng.integers(0, 4))):
+            admit()
+        if step % 5 == 4:
+            k = int(rng.integers(1, 20))
+            assert idx.evict(k) == orc.evict(k)
+            assert eng.compact() == len(ref.compact())
+        check()
+
+
+@pytest.mark.parametrize("mode", ["reference", "suffix"])
+def test_reference_publish_lets_eviction_free_pinned_blocks(mode):
+    """The reference publishes a finished sequence's whole chain under its hit
+    node (engine.py:201 -> radix_kv.py:187); evicting that duplicate node
+    frees the hit path's blocks while another sequence still pins them.
+    ``publish_mode="suffix"`` publishes only the part past the hit."""
+    from chenxing_b200.engine import BatchedKVEngine
+    idx = RadixIndex(32, 4, clock=logical_clock())
+    eng = BatchedKVEngine(idx, n_q_heads=1, publish_mode=mode)
+    prefix = list(range(100, 108))                       # two whole blocks
+    t = []
+    grow_table(idx, t, 8)
+    idx.insert(prefix, t)
+    eng.add(1, prefix + [1, 2, 3, 4, 5])
+    eng.add(2, prefix + [9, 9, 9, 9, 9])
+    for sid in (1, 2):
+        eng.commit(eng.plan_host([sid], [5]))
+    pinned = eng.seqs[1].block_table[:2]
+    eng.finish(2)
+    idx.evict(1)
+    freed = [b for b in pinned if b in idx._free]
+    assert bool(freed) == (mode == "reference")
