@@ -26,7 +26,8 @@ DEV_FLAG_NAMES = {1: "bad slot", 2: "bad block id", 4: "context longer than its 
 
 EXPORTS = ("cx_version", "cx_last_error", "cx_device_error", "cx_kv_append", "cx_kv_gather",
            "cx_block_copy", "cx_paged_workspace_bytes", "cx_paged_decode", "cx_paged_verify",
-           "cx_attention_dense", "cx_paged_decode_static")
+           "cx_attention_dense", "cx_paged_decode_static", "cx_paged_kernel_kind")
+KERNEL_KINDS = {0: "generic", 1: "mma", 2: "tcgen05"}
 
 
 class CxPool(ctypes.Structure):
@@ -71,6 +72,8 @@ _SIGS = {
                             _I32, _I64, _VP, ctypes.c_float, _VP, _VP], ctypes.c_int),
     "cx_paged_decode_static": ([ctypes.POINTER(CxPool), _I64, ctypes.POINTER(CxAttnBatch), _VP,
                                 _I32, _VP, _VP], ctypes.c_int),
+    "cx_paged_kernel_kind": ([ctypes.POINTER(CxPool), ctypes.POINTER(CxAttnBatch), _I32, _I32],
+                             ctypes.c_int),
 }
 
 

@@ -129,6 +129,12 @@ class PagedBatch:
             return int(np.sum(self.ctx_host - lo))
         return int(self.ctx_host.sum())
 
+    def kernel_kind(self, q_dtype=torch.bfloat16) -> str:
+        """Which libcxkv kernel attends this batch: "generic", "mma" or "tcgen05"."""
+        k = _lib.lib().cx_paged_kernel_kind(self.cache.cx_pool(), self._c,
+                                            _lib.cx_dtype(q_dtype), int(self.verify))
+        return _lib.KERNEL_KINDS[k]
+
     def c_struct(self) -> _lib.CxAttnBatch:
         return self._c
 

@@ -615,6 +615,12 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
     }
 }
 
+}  // namespace cx
+
+#include "attn_prefill_tc.cuh"
+
+namespace cx {
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -749,6 +755,41 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
     cx_attn_batch b = *bt;
     b.max_q_len = max_q;
 
+    if (tc_eligible(pool, &b, q_dtype)) {
+        // packed query tile >= 64 rows: tcgen05 kernel, no workspace
+        const int G = (int)(b.n_q_heads / pool->n_kv_heads);
+        TcParams t{};
+        t.tables = b.block_tables;
+        t.table_stride = b.table_stride;
+        t.ctx_lens = b.ctx_lens;
+        t.q_start = b.q_start;
+        t.batch = (int)b.batch;
+        t.hk = (int)pool->n_kv_heads;
+        t.hq = (int)b.n_q_heads;
+        t.group = G;
+        t.tpt = kTcRows / G;
+        t.n_qtiles = (int)((max_q + t.tpt - 1) / t.tpt);
+        t.n_blocks = (int)pool->n_blocks;
+        t.layer = (int)layer;
+        t.window = b.window > 0 ? (int)(b.window < (1ll << 30) ? b.window : (1ll << 30)) : 0;
+        t.scale_log2 = scale * 1.4426950408889634f;
+        t.q = q;
+        t.out = out;
+        if (b.table_stride > (1ll << 26) || pool->n_blocks > INT32_MAX / pool->n_kv_heads ||
+            (int64_t)pool->n_layers * pool->n_blocks * pool->n_kv_heads > INT32_MAX)
+            return fail(CX_ERR_UNSUPPORTED, "paged attention: pool or table too large");
+        CUtensorMap tk, tv;
+        rc = make_pool_tmap(&tk, pool->k, pool, 1);
+        if (rc) return rc;
+        rc = make_pool_tmap(&tv, pool->v, pool, 1);
+        if (rc) return rc;
+        if (pool->head_dim == 128)
+            return q_dtype == CX_F32 ? launch_tc<128, float>(tk, tv, t, st)
+                                     : launch_tc<128, __nv_bfloat16>(tk, tv, t, st);
+        return q_dtype == CX_F32 ? launch_tc<64, float>(tk, tv, t, st)
+                                 : launch_tc<64, __nv_bfloat16>(tk, tv, t, st);
+    }
+
     if (!mma_eligible(pool, &b, q_dtype)) {
         GenericParams g{};
         g.q = q;
@@ -839,6 +880,17 @@ size_t cx_paged_workspace_bytes(const cx_pool* pool, const cx_attn_batch* b) {
     const int64_t G = b->n_q_heads / pool->n_kv_heads;
     const int64_t max_q = b->q_start ? (b->max_q_len > 0 ? b->max_q_len : 1) : 1;
     return ws_layout(b->batch, pool->n_kv_heads, G * max_q, pool->head_dim, grid_size()).total;
+}
+
+int cx_paged_kernel_kind(const cx_pool* pool, const cx_attn_batch* batch, int32_t q_dtype,
+                         int32_t verify) {
+    using namespace cx;
+    if (!pool || !batch || pool->n_kv_heads <= 0) return CX_KERNEL_GENERIC;
+    cx_attn_batch b = *batch;
+    b.max_q_len = verify ? (b.max_q_len > 0 ? b.max_q_len : 1) : 1;
+    if (tc_eligible(pool, &b, q_dtype)) return CX_KERNEL_TCGEN05;
+    if (mma_eligible(pool, &b, q_dtype)) return CX_KERNEL_MMA;
+    return CX_KERNEL_GENERIC;
 }
 
 int cx_paged_decode(const cx_pool* pool, int64_t layer, const cx_attn_batch* batch, const void* q,

@@ -172,6 +172,17 @@ int cx_paged_verify(const cx_pool* pool, int64_t layer, const cx_attn_batch* bat
 int cx_paged_decode_static(const cx_pool* pool, int64_t layer, const cx_attn_batch* batch,
                            const void* q, int32_t q_dtype, float* out, void* stream);
 
+/* Which kernel cx_paged_decode (verify = 0) or cx_paged_verify (verify = 1)
+ * runs for this pool, batch shape and query type — diagnostics, no
+ * counterpart in the reference: CX_KERNEL_GENERIC (fp32 / fp16 pools, other
+ * block sizes or head dims: exact CUDA-core kernel), CX_KERNEL_MMA (bf16
+ * pool, packed query tile of 1..63 rows: TMA + mma.sync split-K kernel) or
+ * CX_KERNEL_TCGEN05 (bf16 pool, packed tile of 64 rows or more: TMA +
+ * tcgen05 / TMEM kernel).  Reads only the host fields of `batch`. */
+enum { CX_KERNEL_GENERIC = 0, CX_KERNEL_MMA = 1, CX_KERNEL_TCGEN05 = 2 };
+int cx_paged_kernel_kind(const cx_pool* pool, const cx_attn_batch* batch, int32_t q_dtype,
+                         int32_t verify);
+
 /* Dense attention — replaces flash_attention / naive_attention on contiguous
  * arrays (chenxing/core/attention.py:43-148): q [b][hq][sq][d],
  * k [b][hk][sk][d], v [b][hk][sk][dv] (kv_dtype), out float32 [b][hq][sq][dv].

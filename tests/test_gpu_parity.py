@@ -234,6 +234,48 @@ def test_verify_ragged_query_lengths():
     case.check(case.run(), rtol=BF16_RTOL)
 
 
+# ---------------------------------------------------------------------------
+# packed query tiles of >= 64 rows: the tcgen05 / TMEM kernel (chunked
+# prefill and long verify chains)
+# ---------------------------------------------------------------------------
+TC_CASES = [
+    dict(hq=32, hk=8, d=128, ctx=[40], q_lens=[16]),
+    dict(hq=32, hk=8, d=128, ctx=[300, 129, 64], q_lens=[16, 32, 64]),
+    dict(hq=32, hk=8, d=128, ctx=[1000, 777], q_lens=[200, 33], window=100),
+    dict(hq=32, hk=8, d=128, ctx=[3000, 1500], q_lens=[1024, 300]),
+    dict(hq=32, hk=8, d=128, ctx=[5000], q_lens=[257], window=4096),
+    dict(hq=32, hk=8, d=64, ctx=[500, 90], q_lens=[70, 20]),
+    dict(hq=8, hk=8, d=128, ctx=[700, 300], q_lens=[300, 64]),
+    dict(hq=16, hk=8, d=128, ctx=[190, 33, 7], q_lens=[40, 33, 0]),
+    dict(hq=64, hk=8, d=128, ctx=[260, 48], q_lens=[40, 8], q_dtype=torch.bfloat16),
+    dict(hq=32, hk=8, d=128, ctx=[2048, 17], q_lens=[128, 17], q_dtype=torch.bfloat16,
+         window=1),
+]
+
+
+@pytest.mark.parametrize("kw", TC_CASES, ids=lambda kw: "-".join(
+    f"{k}{v}" for k, v in kw.items() if k in ("hq", "hk", "d", "window")) + f"-T{max(kw['q_lens'])}")
+def test_prefill_tcgen05_matches_oracle(kw):
+    case = PagedCase(seed=21, **kw)
+    batch = case.batch()
+    assert batch.kernel_kind(case.q_dev.dtype) == "tcgen05"
+    case.check(case.run(batch), rtol=BF16_RTOL)
+
+
+def test_kernel_selection_by_packed_rows():
+    """Decode and short verify chains (< 64 packed rows) stay on the split-K
+    mma.sync kernel; 64 rows and more go to tcgen05; fp32 pools stay on the
+    exact generic kernel."""
+    dec = PagedCase(hq=32, hk=8, d=128, ctx=[100], seed=1)
+    assert dec.batch().kernel_kind() == "mma"
+    short = PagedCase(hq=32, hk=8, d=128, ctx=[100], q_lens=[15], seed=1)
+    assert short.batch().kernel_kind() == "mma"
+    edge = PagedCase(hq=32, hk=8, d=128, ctx=[100], q_lens=[16], seed=1)
+    assert edge.batch().kernel_kind() == "tcgen05"
+    f32 = PagedCase(hq=32, hk=8, d=128, ctx=[100], q_lens=[64], dtype=np.float32, seed=1)
+    assert f32.batch().kernel_kind() == "generic"
+
+
 def test_fp32_pool_paged_decode_and_verify_exact():
     case = PagedCase(hq=8, hk=2, d=64, ctx=[64, 511, 1, 130], dtype="float32", seed=1)
     case.check(case.run(), atol=F32_ATOL)
