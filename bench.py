@@ -45,8 +45,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["cfg2", "small"], default="cfg2",
-                    help="small: 1 layer, pool sized to need (~2 GB, for profiler captures)")
+    ap.add_argument("--config", choices=["cfg2", "small", "prefill", "prefill-small"],
+                    default="cfg2",
+                    help="small: 1 layer, pool sized to need (~2 GB, for profiler captures); "
+                         "prefill: chunked-prefill attention on the tcgen05 kernel (its own "
+                         "JSON line, TFLOP/s); prefill-small: the same, 2 sequences")
     ap.add_argument("--pool-frac", type=float, default=0.9)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -541,12 +544,101 @@ def run_e2e(args, lib, pool, cache, batches, slots, layers, n_sets, dev, world, 
                     "side streams overlapped per layer"}
 
 
+# ---------------------------------------------------------------------------
+# chunked prefill on the tcgen05 kernel (separate mode, not the headline)
+# ---------------------------------------------------------------------------
+PREFILL_T = 1024          # new tokens per sequence in the chunk
+
+
+def run_prefill(args):
+    """Chunked-prefill attention, one launch = one layer: B sequences each
+    append a chunk of PREFILL_T tokens after ctx_prev ~ U[1024, 8192] cached
+    ones and attend causally over ctx_prev + PREFILL_T keys (Hq 32 / Hkv 8,
+    D 128, bf16 pool, bf16 Q).  FLOPs per launch = 4 * Hq * D * sum over
+    sequences of attended (query, key) pairs."""
+    import torch
+    from chenxing_b200 import PagedBatch, RadixPagedKVCache, _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B = 8 if args.config == "prefill" else 2
+    rng = np.random.default_rng(args.seed)
+    ctx_prev = rng.integers(1024, 8193, size=B).astype(np.int64)
+    T = PREFILL_T
+    ctx = ctx_prev + T
+    nb = [int(-(-c // BS)) for c in ctx]
+    n_blocks = sum(nb) + 16
+    perm = rng.permutation(n_blocks)
+    tables, o = [], 0
+    for n in nb:
+        tables.append([int(x) for x in perm[o:o + n]])
+        o += n
+    cache = RadixPagedKVCache(n_blocks, BS, 1, HK, D, dtype="bfloat16", device=dev,
+                              host_io=False)
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed)
+    cache._k.normal_(0.0, 1.0 / math.sqrt(D), generator=g)
+    cache._v.normal_(0.0, 1.0 / math.sqrt(D), generator=g)
+    q = (torch.randn((B * T, HQ, D), device=dev, generator=g) / math.sqrt(D)).bfloat16()
+    out = torch.empty((B * T, HQ, D), dtype=torch.float32, device=dev)
+    batch = PagedBatch(cache, tables, ctx, n_q_heads=HQ, q_lens=[T] * B)
+    kind = batch.kernel_kind(q.dtype)
+    pairs = int(sum(int(cp) * T + T * (T + 1) // 2 for cp in ctx_prev))
+    flops = 4.0 * HQ * D * pairs
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        cache.verify_batch(0, q, batch, out)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(device_uuid(dev))
+    sampler.start()
+    time.sleep(0.5)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for e0, e1 in evs:
+        e0.record(stream)
+        cache.verify_batch(0, q, batch, out)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    flags = _lib.device_flags(clear=True)
+    if flags:
+        raise RuntimeError(f"device flags: {_lib.describe_flags(flags)}")
+    ms = [a.elapsed_time(b) for a, b in evs]
+    avg = float(np.mean(ms))
+    tflops = flops / (avg / 1e3) / 1e12
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, src = float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    except (OSError, KeyError, ValueError):
+        peak, src = 1590.0, "fallback"
+    kv_bytes = int(sum(int(c) for c in ctx)) * UNIT_BYTES     # one layer, K + V
+    line = {"metric": "chunked-prefill paged attention TFLOP/s (tcgen05 kernel)",
+            "value": tflops, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": avg, "higher_is_better": True,
+            "scaling": "none", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"chunked prefill: {B} sequences x {T}-token chunk after "
+                                   f"ctx ~ U[1024, 8192]", "q_heads": HQ, "kv_heads": HK,
+                       "head_dim": D, "block_size": BS, "kernel": kind,
+                       "attended_pairs_per_head": pairs,
+                       "l2": "K/V > 126 MB L2" if kv_bytes > 126e6
+                       else "K/V fits in L2 (small case)"},
+            "roofline": {"bound": "tensor", "kernel": "paged_attn_tc_kernel",
+                         "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tflops / peak, "peak_source": src,
+                         "flops_per_launch": flops, "avg_launch_ms": avg,
+                         "min_launch_ms": float(np.min(ms))},
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.config in ("prefill", "prefill-small"):
+        run_prefill(args)
     else:
         run_ours(args)
 
