@@ -768,7 +768,7 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
         t.hq = (int)b.n_q_heads;
         t.group = G;
         t.tpt = kTcRows / G;
-        t.n_qtiles = (int)((max_q + t.tpt - 1) / t.tpt);
+        t.n_ctiles = (int)((max_q + 2 * t.tpt - 1) / (2 * t.tpt));
         t.n_blocks = (int)pool->n_blocks;
         t.layer = (int)layer;
         t.window = b.window > 0 ? (int)(b.window < (1ll << 30) ? b.window : (1ll << 30)) : 0;

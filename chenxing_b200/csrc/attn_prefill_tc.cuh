@@ -2,45 +2,49 @@
 // chunked prefill and long speculative-verify chains, used when the packed
 // query tile reaches 64 rows (rows = query tokens x GQA group).
 //
-// One CTA owns (sequence b, KV head h, query tile): kTcRows = 128 packed rows,
-// row r = (token t0 + r / G, query head h*G + r % G), so every row of the tile
-// reads the same K/V head and the tile is a dense M = 128 operand.  Keys are
-// walked in tiles of kTcKeys = 128 (eight 16-token pool blocks):
+// One CTA owns (sequence b, KV head h) and two query tiles of kTcRows = 128
+// packed rows each; row r of tile w is (token t0 + w*tpt + r / G, query head
+// h*G + r % G), so every row shares the K/V head and a tile is a dense
+// M = 128 operand even for GQA.  Keys are walked in tiles of kTcKeys = 64
+// (four 16-token pool blocks):
 //
-//   producer warp  : TMA loads of the eight blocks' K and V tiles (two
-//                    128-byte column halves each, 128-byte swizzle) into a
-//                    2-stage ring, completing on mbarriers;
-//   MMA warp       : one elected thread issues S = Q K^T (tcgen05.mma,
-//                    kind::f16, bf16 x bf16 -> fp32, M 128, N 128, K = D) into
-//                    TMEM, then O += P V (K = 128 keys) into a second TMEM
-//                    region, and signals completion with tcgen05.commit;
-//   softmax warps  : 4 warps = 128 threads = the 128 TMEM lanes, so thread r
-//                    owns row r: it reads its S row with tcgen05.ld, applies
-//                    the causal / sliding-window mask, keeps the running max
-//                    and denominator in registers (no shuffles: the whole row
-//                    is in one thread), rescales its O row in TMEM when the
-//                    max moves, and writes P (bf16) to shared memory in the
-//                    swizzled K-major layout the next MMA reads.
+//   producer warp  : TMA loads of the four blocks' K and V tiles (128-byte
+//                    column halves, 128-byte swizzle) into a 3-stage ring;
+//   MMA warp       : one thread issues tcgen05.mma (kind::f16, bf16 x bf16 ->
+//                    fp32) S_w = Q_w K^T into TMEM and O_w += P_w V into TMEM
+//                    for both query tiles w = 0, 1, interleaved so the tensor
+//                    pipe runs one tile's MMAs while the other tile's softmax
+//                    runs: PV_0(i), S_0(i+1), PV_1(i), S_1(i+1), ...;
+//   softmax warps  : one warpgroup per query tile, 128 threads = the 128 TMEM
+//                    lanes, thread r owning row r: tcgen05.ld of its S row,
+//                    causal / sliding-window mask on edge tiles only, running
+//                    max and denominator in registers (no shuffles), lazy O
+//                    rescale in TMEM (only when a row max grows by more than
+//                    2^8; a stale max is exact after the final division by
+//                    the denominator), bf16 P into shared memory in the
+//                    swizzled K-major layout the PV MMA reads.
 //
-// Q is staged once per CTA (bf16, same swizzled layout).  The epilogue reads
-// O from TMEM, divides by the denominator and writes fp32 rows.  Every wait
-// is bounded; on a timeout the CTA raises CX_DEV_WAIT_TIMEOUT, drains its own
-// outstanding copies and MMAs, frees its TMEM and returns.
+// Q is staged once per CTA (bf16, same layout).  The epilogue reads O from
+// TMEM, divides by the denominator and writes fp32 rows.  Every wait is
+// bounded; on a timeout the CTA raises CX_DEV_WAIT_TIMEOUT, drains its own
+// copies and MMAs, frees its TMEM and returns.  tcgen05.ld / tcgen05.st are
+// warp-collective, so every branch around them is decided warp-uniformly.
 #pragma once
 #include "cx_common.cuh"
 
 namespace cx {
 
-constexpr int kTcRows = 128;   // packed query rows per CTA (MMA M)
-constexpr int kTcKeys = 128;   // keys per tile (S: N, PV: K)
-constexpr int kTcStages = 2;
+constexpr int kTcRows = 128;    // packed query rows per query tile (MMA M)
+constexpr int kTcKeys = 64;     // keys per key tile (S: N, PV: K)
+constexpr int kTcStages = 3;
+constexpr float kTcRescaleLog2 = 8.f;   // rescale O only when a row max grows by > 2^8
 
 struct TcParams {
     const int32_t* tables;
     int64_t table_stride;
     const int32_t* ctx_lens;
     const int32_t* q_start;  // NULL: one query row per sequence
-    int32_t batch, hk, hq, group, tpt, n_qtiles, n_blocks, layer, window;
+    int32_t batch, hk, hq, group, tpt, n_ctiles, n_blocks, layer, window;
     float scale_log2;
     const void* q;
     float* out;
@@ -48,23 +52,24 @@ struct TcParams {
 
 template <int D>
 struct TcCfg {
-    static constexpr int HALVES = D / 64;                   // 128-byte column halves
-    static constexpr int HALF_ROWS128 = 128 * 128;          // one half of a 128-row tile
+    static constexpr int HALVES = D / 64;                    // 128-byte column halves
+    static constexpr int Q_HALF = kTcRows * 128;             // 16 KB: 128 rows x 128 B
     static constexpr int Q_BYTES = kTcRows * D * 2;
-    static constexpr int KT_BYTES = kTcKeys * D * 2;        // one K (or V) tile
+    static constexpr int KV_HALF = kTcKeys * 128;            // 8 KB: 64 keys x 128 B
+    static constexpr int KT_BYTES = kTcKeys * D * 2;         // one K (or V) tile
     static constexpr int STAGE = 2 * KT_BYTES;
-    static constexpr int P_BYTES = kTcRows * kTcKeys * 2;
-    static constexpr int OFF_Q = 0;
-    static constexpr int OFF_KV = OFF_Q + Q_BYTES;
-    static constexpr int OFF_P = OFF_KV + kTcStages * STAGE;
-    static constexpr int OFF_BAR = OFF_P + P_BYTES;
-    static constexpr int SMEM = OFF_BAR + 256 + 1024;       // + 1 KB alignment slack
-    // S uses columns [0, 128), O [128, 128 + D); the whole 512-column TMEM is
-    // taken (one CTA per SM: shared memory allows no second one)
+    static constexpr int P_BYTES = kTcRows * kTcKeys * 2;    // 16 KB
+    static constexpr int OFF_Q = 0;                          // 2 query tiles
+    static constexpr int OFF_KV = OFF_Q + 2 * Q_BYTES;
+    static constexpr int OFF_P = OFF_KV + kTcStages * STAGE; // 2 P tiles
+    static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;        // + 1 KB alignment slack
+    // TMEM columns: S_0 [0, 64), S_1 [64, 128), O_0 [128, 128 + D),
+    // O_1 [256, 256 + D); all 512 are taken (one CTA per SM by shared memory)
     static constexpr int TMEM_COLS = 512;
-    static constexpr int THREADS = 192;                     // softmax x4, producer, MMA
-    static constexpr int PRODUCER_WARP = 4;
-    static constexpr int MMA_WARP = 5;
+    static constexpr int THREADS = 320;                      // 2 x 4 softmax, producer, MMA
+    static constexpr int PRODUCER_WARP = 8;
+    static constexpr int MMA_WARP = 9;
 };
 
 // ---- tcgen05 helpers ------------------------------------------------------
@@ -161,12 +166,12 @@ __device__ __forceinline__ void tc_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// Byte offset of element (row, col) of a K-major bf16 tile with 128 rows and
-// 128-byte swizzle: column halves of 64 elements are separate 16 KB regions;
-// inside one, row r is the 128-byte line r and its 16-byte chunk c sits at
-// chunk c ^ (r & 7).
-__device__ __forceinline__ uint32_t tc_swz(int row, int col) {
-    return (uint32_t)((col >> 6) * (128 * 128) + row * 128 +
+// Byte offset of element (row, col) of a K-major bf16 operand tile with
+// 128-byte swizzle: column halves of 64 elements are separate regions of
+// `rows` 128-byte lines; inside one, row r is line r and its 16-byte chunk c
+// sits at chunk c ^ (r & 7).
+__device__ __forceinline__ uint32_t tc_swz(int row, int col, int rows) {
+    return (uint32_t)((col >> 6) * (rows * 128) + row * 128 +
                       ((((col & 63) >> 3) ^ (row & 7)) << 4) + (col & 7) * 2);
 }
 
@@ -182,36 +187,35 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
     unsigned char* skv = sm + C::OFF_KV;
     unsigned char* sp = sm + C::OFF_P;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
-    uint64_t* kv_full = bars;                 // [kTcStages]
-    uint64_t* kv_empty = bars + kTcStages;    // [kTcStages]
-    uint64_t* s_full = bars + 2 * kTcStages;
-    uint64_t* p_full = s_full + 1;
-    uint64_t* o_done = s_full + 2;
-    uint64_t* mma_drain = s_full + 3;          // last commit of the MMA thread
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_full + 4);
+    uint64_t* kv_full = bars;                  // [kTcStages]
+    uint64_t* kv_empty = bars + kTcStages;     // [kTcStages]
+    uint64_t* s_full = bars + 2 * kTcStages;   // [2] S_w ready in TMEM
+    uint64_t* p_full = s_full + 2;             // [2] P_w in smem, O_w rescaled
+    uint64_t* o_done = s_full + 4;             // [2] PV_w completed
+    uint64_t* mma_drain = s_full + 6;          // last commit of the MMA thread
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_full + 7);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
     volatile int* s_issued = s_abort + 1;      // key tiles whose TMA loads were issued
-    volatile int* s_pv = s_abort + 2;          // key tiles whose P V was committed
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int BH = p.batch * p.hk;
-    const int qtile = p.n_qtiles - 1 - (int)(blockIdx.x / BH);  // longest key ranges first
+    const int ctile = p.n_ctiles - 1 - (int)(blockIdx.x / BH);  // longest key ranges first
     const int rem = (int)(blockIdx.x % BH);
     const int b = rem / p.hk, h = rem % p.hk;
-    const int G = p.group;
+    const int G = p.group, tpt = p.tpt;
 
     const int qs = p.q_start ? p.q_start[b] : b;
     const int T = p.q_start ? p.q_start[b + 1] - qs : 1;
-    const int t0 = qtile * p.tpt;
+    const int t0 = ctile * 2 * tpt;            // first token of query tile 0
     if (t0 >= T) return;
-    const int t1 = min(T, t0 + p.tpt);
+    const int nq = t0 + tpt < T ? 2 : 1;        // query tiles with valid rows
+    const int t_end = min(T, t0 + nq * tpt);
     const int cap = (int)(p.table_stride * kBlockTok);
     const int ctx = min(max(p.ctx_lens[b], 0), cap);
     const int pos0 = ctx - T;                  // position of query token 0
-    const int pos_lo = pos0 + t0, pos_hi = pos0 + t1 - 1;
-    const int key_hi = min(pos_hi, ctx - 1);
+    const int key_hi = min(pos0 + t_end - 1, ctx - 1);
     int key_lo = 0;
-    if (p.window > 0) key_lo = max(0, pos_lo - p.window + 1);
+    if (p.window > 0) key_lo = max(0, pos0 + t0 - p.window + 1);
     const int kb0 = key_lo / kBlockTok;
     const int n_tiles = key_hi >= key_lo ? (key_hi - kb0 * kBlockTok) / kTcKeys + 1 : 0;
     const int nblk_seq = (ctx + kBlockTok - 1) / kBlockTok;
@@ -221,16 +225,16 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        mbar_init(s_full, 1);
-        mbar_init(p_full, 128);
-        mbar_init(o_done, 1);
+        for (int w = 0; w < 2; ++w) {
+            mbar_init(&s_full[w], 1);
+            mbar_init(&p_full[w], 128);
+            mbar_init(&o_done[w], 1);
+        }
         mbar_init(mma_drain, 1);
         *s_abort = 0;
         *s_issued = 0;
-        *s_pv = 0;
         fence_mbar_init();
     }
-    // TMEM: S in columns [0, 128), O in [128, 128 + D)
     if (warp == C::MMA_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_addr(s_tmem)),
@@ -238,23 +242,25 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    // Q tile -> shared memory (bf16, swizzled K-major), rows past the chunk zeroed
-    if (warp < 4) {
-        const int r = tid;
-        const int t = t0 + r / G;
+    // Q tiles -> shared memory (bf16, swizzled K-major); rows past the chunk are zero
+    if (warp < 8) {
+        const int w = warp >> 2, r = tid & 127;
+        const int t = t0 + w * tpt + r / G;
         const int head = h * G + r % G;
-        const bool ok = t < t1;
+        const bool ok = t < t_end;
         const QT* src = static_cast<const QT*>(p.q) + ((int64_t)(qs + t) * p.hq + head) * D;
+        unsigned char* qdst = sq + w * C::Q_BYTES;
 #pragma unroll 4
         for (int c = 0; c < D / 8; ++c) {
-            uint32_t w[4] = {0u, 0u, 0u, 0u};
+            uint32_t wv[4] = {0u, 0u, 0u, 0u};
             if (ok) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
-                    w[e] = pack_bf16(Conv<QT>::to_f(src[c * 8 + 2 * e]),
-                                     Conv<QT>::to_f(src[c * 8 + 2 * e + 1]));
+                    wv[e] = pack_bf16(Conv<QT>::to_f(src[c * 8 + 2 * e]),
+                                      Conv<QT>::to_f(src[c * 8 + 2 * e + 1]));
             }
-            *reinterpret_cast<uint4*>(sq + tc_swz(r, c * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(qdst + tc_swz(r, c * 8, kTcRows)) =
+                make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
         fence_async_smem();
     }
@@ -262,7 +268,6 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-    const uint32_t tm_s = tmem, tm_o = tmem + 128;
 
     if (warp == C::PRODUCER_WARP) {
         // ---------------- TMA producer ----------------
@@ -282,7 +287,7 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
                 mbar_arrive_expect_tx(&kv_full[s], C::STAGE);
                 unsigned char* kd = skv + s * C::STAGE;
                 unsigned char* vd = kd + C::KT_BYTES;
-#pragma unroll 1
+#pragma unroll
                 for (int j = 0; j < kTcKeys / kBlockTok; ++j) {
                     const int blk = kb0 + i * (kTcKeys / kBlockTok) + j;
                     int id = blk < nblk_seq ? tab[blk] : first_id;
@@ -293,9 +298,9 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
                     const int z = (p.layer * p.n_blocks + id) * p.hk + h;
 #pragma unroll
                     for (int hf = 0; hf < C::HALVES; ++hf) {
-                        tma_load_3d(kd + hf * C::HALF_ROWS128 + j * 2048, &tmk, &kv_full[s],
+                        tma_load_3d(kd + hf * C::KV_HALF + j * 2048, &tmk, &kv_full[s],
                                     hf * 64, 0, z);
-                        tma_load_3d(vd + hf * C::HALF_ROWS128 + j * 2048, &tmv, &kv_full[s],
+                        tma_load_3d(vd + hf * C::KV_HALF + j * 2048, &tmv, &kv_full[s],
                                     hf * 64, 0, z);
                     }
                 }
@@ -308,72 +313,99 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
             constexpr uint32_t idesc_s = tc_idesc(kTcRows, kTcKeys, 0);
             constexpr uint32_t idesc_o = tc_idesc(kTcRows, D, 1);
             const uint32_t q_base = smem_addr(sq), p_base = smem_addr(sp);
-            for (int i = 0; i < n_tiles; ++i) {
-                const int s = i % kTcStages;
-                if (!mbar_wait_bounded(&kv_full[s], (i / kTcStages) & 1, s_abort,
-                                       kWaitLimitNs)) {
-                    *s_abort = 1;
-                    raise_flag(CX_DEV_WAIT_TIMEOUT);
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t k_base = smem_addr(skv + s * C::STAGE);
-                const uint32_t v_base = k_base + C::KT_BYTES;
-                // S = Q K^T : K = D in steps of 16 (32 bytes inside a 128-byte row)
+            bool ok = true;
+            // S_w(i) = Q_w K(i)^T : K = D in steps of 16 (32 bytes of a 128-byte line)
+            auto issue_s = [&](int w, int i) {
+                const uint32_t k_base = smem_addr(skv + (i % kTcStages) * C::STAGE);
+                const uint32_t qw = q_base + w * C::Q_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * C::HALF_ROWS128 + (kk & 3) * 32;
-                    tc_mma(tm_s, tc_sdesc(q_base + off, 16, 1024),
-                           tc_sdesc(k_base + off, 16, 1024), idesc_s, kk > 0);
+                    tc_mma(tmem + w * kTcKeys,
+                           tc_sdesc(qw + (kk >> 2) * C::Q_HALF + (kk & 3) * 32, 16, 1024),
+                           tc_sdesc(k_base + (kk >> 2) * C::KV_HALF + (kk & 3) * 32, 16, 1024),
+                           idesc_s, kk > 0);
                 }
-                tc_commit(s_full);
-                if (!mbar_wait_bounded(p_full, i & 1, s_abort, kWaitLimitNs)) {
-                    *s_abort = 1;
-                    raise_flag(CX_DEV_WAIT_TIMEOUT);
-                    break;
-                }
-                tc_fence_after();
-                // O += P V : K = 128 keys in steps of 16 (P: K-major, V: MN-major,
-                // 64-column halves of V 16 KB apart, 8-key groups 1 KB apart)
+                tc_commit(&s_full[w]);
+            };
+            // O_w += P_w V(i) : K = 64 keys in steps of 16; P K-major, V MN-major
+            // (64-column halves of V KV_HALF apart, 8-key groups 1 KB apart)
+            auto issue_pv = [&](int w, int i) {
+                const uint32_t v_base =
+                    smem_addr(skv + (i % kTcStages) * C::STAGE) + C::KT_BYTES;
+                const uint32_t pw = p_base + w * C::P_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < kTcKeys / 16; ++kk) {
-                    const uint32_t poff = (kk >> 2) * C::HALF_ROWS128 + (kk & 3) * 32;
-                    tc_mma(tm_o, tc_sdesc(p_base + poff, 16, 1024),
-                           tc_sdesc(v_base + kk * 2048, C::HALF_ROWS128, 1024), idesc_o,
+                    tc_mma(tmem + 128 + w * 128, tc_sdesc(pw + kk * 32, 16, 1024),
+                           tc_sdesc(v_base + kk * 2048, C::KV_HALF, 1024), idesc_o,
                            (i > 0 || kk > 0) ? 1u : 0u);
                 }
-                tc_commit(o_done);
-                tc_commit(&kv_empty[s]);
-                *s_pv = i + 1;
+                tc_commit(&o_done[w]);
+            };
+            auto wait_kv = [&](int i) {
+                const bool r = mbar_wait_bounded(&kv_full[i % kTcStages],
+                                                 (i / kTcStages) & 1, s_abort, kWaitLimitNs);
+                if (r) tc_fence_after();
+                return r;
+            };
+            auto wait_p = [&](int w, int i) {
+                const bool r = mbar_wait_bounded(&p_full[w], i & 1, s_abort, kWaitLimitNs);
+                if (r) tc_fence_after();
+                return r;
+            };
+            if (n_tiles > 0) {
+                ok = wait_kv(0);
+                if (ok) {
+                    issue_s(0, 0);
+                    if (nq == 2) issue_s(1, 0);
+                }
+            }
+            for (int i = 0; ok && i < n_tiles; ++i) {
+                const bool more = i + 1 < n_tiles;
+                if (!(ok = wait_p(0, i))) break;
+                issue_pv(0, i);
+                if (more) {
+                    if (!(ok = wait_kv(i + 1))) break;
+                    issue_s(0, i + 1);
+                }
+                if (nq == 2) {
+                    if (!(ok = wait_p(1, i))) break;
+                    issue_pv(1, i);
+                    if (more) issue_s(1, i + 1);
+                }
+                tc_commit(&kv_empty[i % kTcStages]);
+            }
+            if (!ok) {
+                *s_abort = 1;
+                raise_flag(CX_DEV_WAIT_TIMEOUT);
             }
             tc_commit(mma_drain);   // completes once every MMA issued above has
         }
-    } else {
-        // ---------------- softmax / correction / epilogue (warps 0-3) ----------------
-        const int r = tid;                      // TMEM lane = packed row
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        const int t = t0 + r / G;
+    } else if (warp < 4 * nq) {
+        // ---------------- softmax / correction / epilogue (warpgroup w) ----------------
+        const int w = warp >> 2, r = tid & 127;
+        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t tm_s = tmem + w * kTcKeys + lane_off;
+        const uint32_t tm_o = tmem + 128 + w * 128 + lane_off;
+        unsigned char* pw = sp + w * C::P_BYTES;
+        const int tw0 = t0 + w * tpt;                            // first token of this tile
+        const int tw1 = min(t_end, tw0 + tpt);
+        const int t = tw0 + r / G;
         const int pos = pos0 + t;
+        const int pos_lo = pos0 + tw0, pos_hi = pos0 + max(tw1, tw0 + 1) - 1;
         const int win = p.window;
         const float sl2 = p.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        // tcgen05.ld / tcgen05.st are warp-collective (.sync.aligned): every
-        // branch around them below is decided warp-uniformly (__all_sync /
-        // __any_sync), including the give-up paths of the bounded waits.
         for (int i = 0; i < n_tiles; ++i) {
-            if (!__all_sync(0xffffffffu, mbar_wait_bounded(s_full, i & 1, s_abort,
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[w], i & 1, s_abort,
                                                             kWaitLimitNs))) {
-                *s_abort = 1;
-                raise_flag(CX_DEV_WAIT_TIMEOUT);
                 ok = false;
                 break;
             }
             tc_fence_after();
             float sv[kTcKeys];
-#pragma unroll
-            for (int c = 0; c < kTcKeys / 32; ++c)
-                tc_ld32(tm_s + lane_off + c * 32, &sv[c * 32]);
+            tc_ld32(tm_s, &sv[0]);
+            tc_ld32(tm_s + 32, &sv[32]);
             tc_wait_ld();
             const int kbase = kb0 * kBlockTok + i * kTcKeys;
             const bool edge = (kbase + kTcKeys - 1 > pos_lo) ||
@@ -394,9 +426,11 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
                     mt = fmaxf(mt, sv[j]);
                 }
             }
-            const float m_new = fmaxf(m, mt);
+            // lazy rescale: keep the reference max unless the row max grew by > 2^8
+            const bool grow = mt > m + kTcRescaleLog2 || (m == -INFINITY && mt > -INFINITY);
+            const float m_new = grow ? mt : m;
             const float m_use = m_new == -INFINITY ? 0.f : m_new;
-            const float alpha = exp2f(m - m_use);
+            const float alpha = grow ? exp2f(m - m_use) : 1.f;
             float sum = 0.f;
 #pragma unroll
             for (int j = 0; j < kTcKeys; ++j) {
@@ -406,11 +440,9 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
             l = l * alpha + sum;
             m = m_new;
             if (i > 0) {
-                // P and O are busy until the previous P V has completed
-                if (!__all_sync(0xffffffffu, mbar_wait_bounded(o_done, (i - 1) & 1, s_abort,
-                                                                kWaitLimitNs))) {
-                    *s_abort = 1;
-                    raise_flag(CX_DEV_WAIT_TIMEOUT);
+                // P_w and O_w are busy until the previous PV_w has completed
+                if (!__all_sync(0xffffffffu, mbar_wait_bounded(&o_done[w], (i - 1) & 1,
+                                                                s_abort, kWaitLimitNs))) {
                     ok = false;
                     break;
                 }
@@ -419,43 +451,43 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
 #pragma unroll 1
                     for (int c = 0; c < D / 32; ++c) {
                         float ov[32];
-                        tc_ld32(tm_o + lane_off + c * 32, ov);
+                        tc_ld32(tm_o + c * 32, ov);
                         tc_wait_ld();
 #pragma unroll
                         for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-                        tc_st32(tm_o + lane_off + c * 32, ov);
+                        tc_st32(tm_o + c * 32, ov);
                     }
                     tc_wait_st();
                 }
             }
 #pragma unroll
             for (int c = 0; c < kTcKeys / 8; ++c) {
-                const uint4 w = make_uint4(pack_bf16(sv[c * 8 + 0], sv[c * 8 + 1]),
-                                           pack_bf16(sv[c * 8 + 2], sv[c * 8 + 3]),
-                                           pack_bf16(sv[c * 8 + 4], sv[c * 8 + 5]),
-                                           pack_bf16(sv[c * 8 + 6], sv[c * 8 + 7]));
-                *reinterpret_cast<uint4*>(sp + tc_swz(r, c * 8)) = w;
+                const uint4 v4 = make_uint4(pack_bf16(sv[c * 8 + 0], sv[c * 8 + 1]),
+                                            pack_bf16(sv[c * 8 + 2], sv[c * 8 + 3]),
+                                            pack_bf16(sv[c * 8 + 4], sv[c * 8 + 5]),
+                                            pack_bf16(sv[c * 8 + 6], sv[c * 8 + 7]));
+                *reinterpret_cast<uint4*>(pw + tc_swz(r, c * 8, kTcRows)) = v4;
             }
             fence_async_smem();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[w]);
         }
         // epilogue
-        const bool row_ok = t < t1;
+        const bool row_ok = t < tw1;
         float* dst = p.out + ((int64_t)(qs + t) * p.hq + h * G + r % G) * D;
         if (n_tiles == 0) {
             if (row_ok)
                 for (int d = 0; d < D; d += 4)
                     *reinterpret_cast<float4*>(dst + d) = make_float4(0.f, 0.f, 0.f, 0.f);
         } else if (__all_sync(0xffffffffu,
-                              ok && mbar_wait_bounded(o_done, (n_tiles - 1) & 1, s_abort,
+                              ok && mbar_wait_bounded(&o_done[w], (n_tiles - 1) & 1, s_abort,
                                                       kWaitLimitNs))) {
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
             for (int c = 0; c < D / 32; ++c) {
                 float ov[32];
-                tc_ld32(tm_o + lane_off + c * 32, ov);
+                tc_ld32(tm_o + c * 32, ov);
                 tc_wait_ld();
                 if (row_ok) {
 #pragma unroll
@@ -466,6 +498,9 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
                 }
             }
         } else {
+            ok = false;
+        }
+        if (!ok) {
             *s_abort = 1;
             raise_flag(CX_DEV_WAIT_TIMEOUT);
         }
@@ -475,13 +510,11 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
     tc_fence_before();
     __syncthreads();
     if (*s_abort && tid == 0) {
-        // wait (bounded) for the loads and MMAs this CTA issued
-        const int issued = *s_issued, pv = *s_pv;
+        const int issued = *s_issued;
         for (int s = 0; s < kTcStages; ++s) {
             const int uses = issued > s ? (issued - 1 - s) / kTcStages + 1 : 0;
             if (uses > 0) mbar_wait_bounded(&kv_full[s], (uses - 1) & 1, nullptr, kWaitLimitNs);
         }
-        (void)pv;
     }
     if (tid == C::MMA_WARP * 32) mbar_wait_bounded(mma_drain, 0, nullptr, kWaitLimitNs);
     __syncthreads();
@@ -495,7 +528,6 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-// Same 3-D pool view as the decode kernel, box of one head: 64 x 16 x 1.
 static bool tc_eligible(const cx_pool* pool, const cx_attn_batch* b, int32_t q_dtype) {
     const int64_t G = b->n_q_heads / pool->n_kv_heads;
     const int64_t rows = G * b->max_q_len;
@@ -514,7 +546,7 @@ static int launch_tc(const CUtensorMap& tk, const CUtensorMap& tv, const TcParam
     auto kern = paged_attn_tc_kernel<D, QT>;
     CX_CUDA_CHECK(
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    const int64_t grid = (int64_t)p.n_qtiles * p.batch * p.hk;
+    const int64_t grid = (int64_t)p.n_ctiles * p.batch * p.hk;
     if (grid <= 0) return CX_OK;
     if (grid > INT32_MAX) return fail(CX_ERR_UNSUPPORTED, "paged attention: grid too large");
     kern<<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(tk, tv, p);
