@@ -9,12 +9,16 @@
 // (four 16-token pool blocks):
 //
 //   producer warp  : TMA loads of the four blocks' K and V tiles (128-byte
-//                    column halves, 128-byte swizzle) into a 3-stage ring;
+//                    column halves, 128-byte swizzle) into a 4-stage ring;
 //   MMA warp       : one thread issues tcgen05.mma (kind::f16, bf16 x bf16 ->
 //                    fp32) S_w = Q_w K^T into TMEM and O_w += P_w V into TMEM
-//                    for both query tiles w = 0, 1, interleaved so the tensor
-//                    pipe runs one tile's MMAs while the other tile's softmax
-//                    runs: PV_0(i), S_0(i+1), PV_1(i), S_1(i+1), ...;
+//                    for both query tiles w = 0, 1: the next tile's scores
+//                    S_w(i+1) as soon as warpgroup w has read S_w(i) into
+//                    registers, PV_w(i) once P_w(i) is written, so the tensor
+//                    pipe computes scores while the softmax runs;
+//   grid           : the query tiles of one (sequence, KV head) are adjacent
+//                    block indices (longest key range first), so the CTAs
+//                    resident at a time share their K/V through L2;
 //   softmax warps  : one warpgroup per query tile, 128 threads = the 128 TMEM
 //                    lanes, thread r owning row r: tcgen05.ld of its S row,
 //                    causal / sliding-window mask on edge tiles only, running
@@ -36,7 +40,7 @@ namespace cx {
 
 constexpr int kTcRows = 128;    // packed query rows per query tile (MMA M)
 constexpr int kTcKeys = 64;     // keys per key tile (S: N, PV: K)
-constexpr int kTcStages = 3;
+constexpr int kTcStages = 4;
 constexpr float kTcRescaleLog2 = 8.f;   // rescale O only when a row max grows by > 2^8
 
 struct TcParams {
@@ -192,16 +196,16 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
     uint64_t* s_full = bars + 2 * kTcStages;   // [2] S_w ready in TMEM
     uint64_t* p_full = s_full + 2;             // [2] P_w in smem, O_w rescaled
     uint64_t* o_done = s_full + 4;             // [2] PV_w completed
-    uint64_t* mma_drain = s_full + 6;          // last commit of the MMA thread
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_full + 7);
+    uint64_t* s_free = s_full + 6;             // [2] S_w read into registers
+    uint64_t* mma_drain = s_full + 8;          // last commit of the MMA thread
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_full + 9);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
     volatile int* s_issued = s_abort + 1;      // key tiles whose TMA loads were issued
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int BH = p.batch * p.hk;
-    const int ctile = p.n_ctiles - 1 - (int)(blockIdx.x / BH);  // longest key ranges first
-    const int rem = (int)(blockIdx.x % BH);
-    const int b = rem / p.hk, h = rem % p.hk;
+    const int bh = (int)(blockIdx.x / p.n_ctiles);
+    const int ctile = p.n_ctiles - 1 - (int)(blockIdx.x % p.n_ctiles);  // longest first
+    const int b = bh / p.hk, h = bh % p.hk;
     const int G = p.group, tpt = p.tpt;
 
     const int qs = p.q_start ? p.q_start[b] : b;
@@ -229,6 +233,7 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
             mbar_init(&s_full[w], 1);
             mbar_init(&p_full[w], 128);
             mbar_init(&o_done[w], 1);
+            mbar_init(&s_free[w], 128);
         }
         mbar_init(mma_drain, 1);
         *s_abort = 0;
@@ -352,6 +357,15 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
                 if (r) tc_fence_after();
                 return r;
             };
+            auto wait_sfree = [&](int w, int i) {
+                const bool r = mbar_wait_bounded(&s_free[w], i & 1, s_abort, kWaitLimitNs);
+                if (r) tc_fence_after();
+                return r;
+            };
+            // Order per key tile i: S_0(i+1), S_1(i+1) as soon as each softmax
+            // warpgroup has read S(i) into registers, then PV_0(i), PV_1(i) as
+            // soon as P(i) is written: the next scores are computed while the
+            // softmax of this tile runs.
             if (n_tiles > 0) {
                 ok = wait_kv(0);
                 if (ok) {
@@ -360,17 +374,20 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
                 }
             }
             for (int i = 0; ok && i < n_tiles; ++i) {
-                const bool more = i + 1 < n_tiles;
+                if (i + 1 < n_tiles) {
+                    if (!(ok = wait_kv(i + 1))) break;
+                    if (!(ok = wait_sfree(0, i))) break;
+                    issue_s(0, i + 1);
+                    if (nq == 2) {
+                        if (!(ok = wait_sfree(1, i))) break;
+                        issue_s(1, i + 1);
+                    }
+                }
                 if (!(ok = wait_p(0, i))) break;
                 issue_pv(0, i);
-                if (more) {
-                    if (!(ok = wait_kv(i + 1))) break;
-                    issue_s(0, i + 1);
-                }
                 if (nq == 2) {
                     if (!(ok = wait_p(1, i))) break;
                     issue_pv(1, i);
-                    if (more) issue_s(1, i + 1);
                 }
                 tc_commit(&kv_empty[i % kTcStages]);
             }
@@ -407,6 +424,8 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
             tc_ld32(tm_s, &sv[0]);
             tc_ld32(tm_s + 32, &sv[32]);
             tc_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&s_free[w]);                   // S_w may be overwritten now
             const int kbase = kb0 * kBlockTok + i * kTcKeys;
             const bool edge = (kbase + kTcKeys - 1 > pos_lo) ||
                               (win > 0 && kbase <= pos_hi - win) || (kbase + kTcKeys > ctx);
