@@ -1,6 +1,8 @@
 // KV pool data movement: slot-mapped append (+ copy-on-write of shared tail
 // blocks), the read_layer gather, and whole/partial block copies.
 // Pool layout: [n_layers][n_blocks][n_kv_heads][block_size][head_dim].
+#include <type_traits>
+
 #include "cx_common.cuh"  // unity build: included from cxkv.cu
 
 namespace cx {
@@ -86,6 +88,103 @@ __global__ void __launch_bounds__(256) kv_append_kernel(
     }
 }
 
+// 8 consecutive elements, loaded / converted / stored as 16-byte (32 for
+// fp32) vectors.  Both pointers are 16-byte aligned (checked on the host).
+template <typename T> struct Vec8;
+template <> struct Vec8<float> {
+    __device__ __forceinline__ static void load(const float* p, float (&x)[8]) {
+        const float4 a = reinterpret_cast<const float4*>(p)[0];
+        const float4 b = reinterpret_cast<const float4*>(p)[1];
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    }
+    __device__ __forceinline__ static void store(float* p, const float (&x)[8]) {
+        reinterpret_cast<float4*>(p)[0] = make_float4(x[0], x[1], x[2], x[3]);
+        reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
+    }
+};
+template <typename H> struct Vec8Half {
+    __device__ __forceinline__ static void load(const H* p, float (&x)[8]) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p);
+        const H* e = reinterpret_cast<const H*>(&u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = Conv<H>::to_f(e[i]);
+    }
+    __device__ __forceinline__ static void store(H* p, const float (&x)[8]) {
+        uint4 u;
+        H* e = reinterpret_cast<H*>(&u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) e[i] = Conv<H>::from_f(x[i]);
+        *reinterpret_cast<uint4*>(p) = u;
+    }
+};
+template <> struct Vec8<__nv_bfloat16> : Vec8Half<__nv_bfloat16> {};
+template <> struct Vec8<__half> : Vec8Half<__half> {};
+
+// Vector form of the token rows of kv_append_kernel (no copy-on-write jobs).
+// A CTA walks tokens t = blockIdx.x, blockIdx.x + gridDim.x, ...; its threads
+// own fixed 8-element chunks of a token's rows (ordered head, K|V, chunk, so
+// a warp writes whole contiguous rows), and each thread keeps kUnroll tokens'
+// loads in flight before storing.  Same rounding as the scalar kernel (to
+// float, then round-to-nearest-even to the pool type).  The host guarantees
+// n_blocks * block_size < 2^31 (32-bit slot arithmetic).
+template <typename S, typename P>
+__global__ void __launch_bounds__(256) kv_append_vec_kernel(
+    P* __restrict__ kp, P* __restrict__ vp, PoolGeom g, int64_t layer,
+    const S* __restrict__ kn, const S* __restrict__ vn, const int64_t* __restrict__ slots,
+    int64_t n_tok) {
+    // same element type: move raw 16-byte words (no conversion, fewer
+    // registers, more tokens in flight); otherwise convert through float
+    constexpr bool kRaw = std::is_same<S, P>::value && sizeof(S) == 2;
+    constexpr int kUnroll = kRaw ? 8 : 4;
+    const int H = (int)g.n_kv_heads, D = (int)g.head_dim;
+    const int cpr = D / 8;                              // chunks per row
+    const int per_tok = H * 2 * cpr;
+    const uint32_t bs = (uint32_t)g.block_size;
+    const int64_t cap = g.n_blocks * g.block_size;
+    for (int c0 = threadIdx.x; c0 < per_tok; c0 += blockDim.x) {
+        const int h = c0 / (2 * cpr);
+        const int r = c0 - h * 2 * cpr;
+        const bool is_v = r >= cpr;
+        const int c = is_v ? r - cpr : r;
+        const S* src = (is_v ? vn : kn) + (int64_t)h * D + c * 8;
+        P* dstp = (is_v ? vp : kp) + g.tile(layer, 0, h) + c * 8;
+        const int64_t blk_stride = g.n_kv_heads * g.block_size * g.head_dim;
+        for (int64_t t0 = blockIdx.x; t0 < n_tok; t0 += (int64_t)gridDim.x * kUnroll) {
+            float x[kRaw ? 1 : kUnroll][8];
+            uint4 raw[kRaw ? kUnroll : 1];
+            int64_t dst[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int64_t t = t0 + (int64_t)u * gridDim.x;
+                dst[u] = -1;
+                if (t < n_tok) {
+                    const int64_t slot = slots[t];
+                    if (slot >= cap) {
+                        if (c0 == 0) raise_flag(CX_DEV_BAD_SLOT);
+                    } else if (slot >= 0) {
+                        const uint32_t blk = (uint32_t)slot / bs;
+                        const uint32_t off = (uint32_t)slot - blk * bs;
+                        dst[u] = (int64_t)blk * blk_stride + (int64_t)off * D;
+                        if constexpr (kRaw)
+                            raw[u] = *reinterpret_cast<const uint4*>(src + t * H * D);
+                        else
+                            Vec8<S>::load(src + t * H * D, x[u]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                if (dst[u] < 0) continue;
+                if constexpr (kRaw)
+                    *reinterpret_cast<uint4*>(dstp + dst[u]) = raw[u];
+                else
+                    Vec8<P>::store(dstp + dst[u], x[u]);
+            }
+        }
+    }
+}
+
 // One warp per (token, head) row of the output.
 __global__ void __launch_bounds__(256) kv_gather_kernel(
     const char* __restrict__ kp, const char* __restrict__ vp, PoolGeom g, int64_t layer,
@@ -158,6 +257,18 @@ template <typename S, typename P>
 static void launch_append(const cx_pool* p, int64_t layer, const void* k, const void* v,
                           const int64_t* slots, int64_t n_tok, const int32_t* cs,
                           const int32_t* cd, const int32_t* cn, int64_t n_cow, cudaStream_t st) {
+    const uintptr_t al = reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+                         reinterpret_cast<uintptr_t>(p->k) | reinterpret_cast<uintptr_t>(p->v);
+    if (n_cow == 0 && p->head_dim % 8 == 0 && (al & 15) == 0 &&
+        p->n_blocks * p->block_size < (1ll << 31) &&
+        p->n_kv_heads * 2 * (p->head_dim / 8) <= (1 << 20)) {
+        int64_t blocks = n_tok < (int64_t)num_sms() * 16 ? n_tok : (int64_t)num_sms() * 16;
+        if (blocks < 1) blocks = 1;
+        kv_append_vec_kernel<S, P><<<(unsigned)blocks, 256, 0, st>>>(
+            static_cast<P*>(p->k), static_cast<P*>(p->v), geom_of(p), layer,
+            static_cast<const S*>(k), static_cast<const S*>(v), slots, n_tok);
+        return;
+    }
     const int64_t jobs = (n_tok + n_cow) * p->n_kv_heads;
     kv_append_kernel<S, P><<<grid_for(jobs, 8), 256, 0, st>>>(
         static_cast<P*>(p->k), static_cast<P*>(p->v), geom_of(p), layer,
