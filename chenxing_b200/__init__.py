@@ -10,8 +10,10 @@ from .attention import flash_attention, gqa_expand, naive_attention
 from .batch import PagedBatch, decode_batch, slot_mapping, verify_batch
 from .engine import BatchedKVEngine
 from .radix_kv import OutOfKVCacheError, PrefixHit, RadixIndex, RadixPagedKVCache
+from .rope import RopeTables, build_rope_cache
 from .tensor import CausalMask
 
 __all__ = ["RadixPagedKVCache", "RadixIndex", "PrefixHit", "OutOfKVCacheError",
            "flash_attention", "naive_attention", "gqa_expand", "CausalMask",
-           "PagedBatch", "decode_batch", "verify_batch", "slot_mapping", "BatchedKVEngine"]
+           "PagedBatch", "decode_batch", "verify_batch", "slot_mapping", "BatchedKVEngine",
+           "RopeTables", "build_rope_cache"]

@@ -22,11 +22,13 @@ CX_OK, CX_ERR_RANGE, CX_ERR_SHAPE, CX_ERR_CUDA, CX_ERR_DTYPE, CX_ERR_UNSUPPORTED
 CX_F32, CX_BF16, CX_F16 = 0, 1, 2
 # device flag bits
 DEV_FLAG_NAMES = {1: "bad slot", 2: "bad block id", 4: "context longer than its block table",
-                  8: "pipeline wait timeout", 16: "bad query length"}
+                  8: "pipeline wait timeout", 16: "bad query length",
+                  32: "RoPE position outside the table"}
 
 EXPORTS = ("cx_version", "cx_last_error", "cx_device_error", "cx_kv_append", "cx_kv_gather",
            "cx_block_copy", "cx_paged_workspace_bytes", "cx_paged_decode", "cx_paged_verify",
-           "cx_attention_dense", "cx_paged_decode_static", "cx_paged_kernel_kind")
+           "cx_attention_dense", "cx_paged_decode_static", "cx_paged_kernel_kind",
+           "cx_kv_append_rope")
 KERNEL_KINDS = {0: "generic", 1: "mma", 2: "tcgen05"}
 
 
@@ -74,6 +76,8 @@ _SIGS = {
                                 _I32, _VP, _VP], ctypes.c_int),
     "cx_paged_kernel_kind": ([ctypes.POINTER(CxPool), ctypes.POINTER(CxAttnBatch), _I32, _I32],
                              ctypes.c_int),
+    "cx_kv_append_rope": ([ctypes.POINTER(CxPool), _I64, _VP, _VP, _I32, _VP, _VP, _I64, _VP, _VP,
+                           _I64, _I32, _VP, _I64, _VP, _I32, _VP], ctypes.c_int),
 }
 
 

@@ -185,6 +185,79 @@ __global__ void __launch_bounds__(256) kv_append_vec_kernel(
     }
 }
 
+// RoPE + append: one thread per rotation pair of one row of one token; a
+// token's rows are [Q heads | K heads | V heads].  Pair j is (j, j + D/2)
+// (half-split) or (2j, 2j + 1) (interleaved).  Products and sums use the
+// _rn intrinsics so no multiply-add is contracted: each output is the fp32
+// value the reference's NumPy expression produces.
+__device__ __forceinline__ void rope_pair(float a, float b, const float* c, const float* s,
+                                          int j, int half, bool inter, float& oa, float& ob) {
+    if (inter) {
+        oa = __fsub_rn(__fmul_rn(a, c[j]), __fmul_rn(b, s[j]));
+        ob = __fadd_rn(__fmul_rn(a, s[j]), __fmul_rn(b, c[j]));
+    } else {
+        oa = __fadd_rn(__fmul_rn(a, c[j]), __fmul_rn(-b, s[j]));
+        ob = __fadd_rn(__fmul_rn(b, c[j + half]), __fmul_rn(a, s[j + half]));
+    }
+}
+
+template <typename S, typename P, typename QO>
+__global__ void __launch_bounds__(256) kv_append_rope_kernel(
+    P* __restrict__ kp, P* __restrict__ vp, PoolGeom g, int64_t layer,
+    const S* __restrict__ kn, const S* __restrict__ vn, const int64_t* __restrict__ slots,
+    const int64_t* __restrict__ positions, int64_t n_tok, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, int64_t rows, int inter, const S* __restrict__ q,
+    int hq, QO* __restrict__ q_out) {
+    const int H = (int)g.n_kv_heads, D = (int)g.head_dim, half = D / 2;
+    const int rows_tok = hq + 2 * H;
+    const int64_t per_tok = (int64_t)rows_tok * half;
+    const int64_t total = n_tok * per_tok;
+    const int64_t cap = g.n_blocks * g.block_size;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / per_tok;
+        const int rem = (int)(i - t * per_tok);
+        const int row = rem / half, j = rem - row * half;
+        const int64_t pos = positions[t];
+        if (pos < 0 || pos >= rows) {
+            if (rem == 0) raise_flag(CX_DEV_BAD_POSITION);
+            continue;
+        }
+        const int ia = inter ? 2 * j : j, ib = inter ? 2 * j + 1 : j + half;
+        if (row < hq) {                                   // Q -> q_out
+            const S* x = q + (t * hq + row) * D;
+            float oa, ob;
+            rope_pair(Conv<S>::to_f(x[ia]), Conv<S>::to_f(x[ib]), cos_t + pos * D,
+                      sin_t + pos * D, j, half, inter, oa, ob);
+            QO* y = q_out + (t * hq + row) * D;
+            y[ia] = Conv<QO>::from_f(oa);
+            y[ib] = Conv<QO>::from_f(ob);
+            continue;
+        }
+        const int64_t slot = slots[t];
+        if (slot < 0) continue;                           // padding token
+        if (slot >= cap) {
+            if (rem == 0) raise_flag(CX_DEV_BAD_SLOT);
+            continue;
+        }
+        const bool is_v = row >= hq + H;
+        const int h = row - hq - (is_v ? H : 0);
+        const int64_t dst = g.tile(layer, slot / g.block_size, h) + (slot % g.block_size) * D;
+        const S* x = (is_v ? vn : kn) + (t * H + h) * D;
+        const float a = Conv<S>::to_f(x[ia]), b = Conv<S>::to_f(x[ib]);
+        P* y = (is_v ? vp : kp) + dst;
+        if (is_v) {
+            y[ia] = Conv<P>::from_f(a);
+            y[ib] = Conv<P>::from_f(b);
+        } else {
+            float oa, ob;
+            rope_pair(a, b, cos_t + pos * D, sin_t + pos * D, j, half, inter, oa, ob);
+            y[ia] = Conv<P>::from_f(oa);
+            y[ib] = Conv<P>::from_f(ob);
+        }
+    }
+}
+
 // One warp per (token, head) row of the output.
 __global__ void __launch_bounds__(256) kv_gather_kernel(
     const char* __restrict__ kp, const char* __restrict__ vp, PoolGeom g, int64_t layer,
@@ -315,6 +388,60 @@ int cx_kv_append(const cx_pool* pool, int64_t layer, const void* k_new, const vo
         case CX_F16: return dispatch_append_src<__half>(src_dtype, pool, layer, k_new, v_new, slot_mapping, n_tokens, cow_src, cow_dst, cow_n_valid, n_cow, st);
         default: return fail(CX_ERR_DTYPE, "cx_kv_append: unknown pool dtype");
     }
+}
+
+int cx_kv_append_rope(const cx_pool* pool, int64_t layer, const void* k_new, const void* v_new,
+                      int32_t src_dtype, const int64_t* slot_mapping, const int64_t* positions,
+                      int64_t n_tokens, const float* cos_table, const float* sin_table,
+                      int64_t table_rows, int32_t interleaved, const void* q,
+                      int64_t n_q_heads, void* q_out, int32_t q_out_dtype, void* stream) {
+    using namespace cx;
+    int rc = check_pool(pool);
+    if (rc) return rc;
+    if (layer < 0 || layer >= pool->n_layers)
+        return fail(CX_ERR_RANGE, "cx_kv_append_rope: layer out of range");
+    if (n_tokens < 0 || n_q_heads < 0 || table_rows < 0)
+        return fail(CX_ERR_SHAPE, "cx_kv_append_rope: negative count");
+    if (pool->head_dim % 2 != 0)
+        return fail(CX_ERR_SHAPE, "cx_kv_append_rope: head_dim must be even");
+    if (n_tokens == 0) return CX_OK;
+    if (!k_new || !v_new || !slot_mapping || !positions || !cos_table || !sin_table)
+        return fail(CX_ERR_SHAPE, "cx_kv_append_rope: NULL array");
+    if (n_q_heads > 0 && (!q || !q_out))
+        return fail(CX_ERR_SHAPE, "cx_kv_append_rope: n_q_heads > 0 needs q and q_out");
+    if (n_q_heads > (1 << 20) || pool->n_kv_heads > (1 << 20))
+        return fail(CX_ERR_UNSUPPORTED, "cx_kv_append_rope: too many heads");
+    if (src_dtype != CX_F32 && src_dtype != CX_BF16)
+        return fail(CX_ERR_DTYPE, "cx_kv_append_rope: source must be CX_F32 or CX_BF16");
+    if (n_q_heads > 0 && q_out_dtype != CX_F32 && q_out_dtype != CX_BF16)
+        return fail(CX_ERR_DTYPE, "cx_kv_append_rope: q_out must be CX_F32 or CX_BF16");
+    const int64_t work = n_tokens * (n_q_heads + 2 * pool->n_kv_heads) * (pool->head_dim / 2);
+    const int grid = grid_for(work, 256);
+    cudaStream_t st = as_stream(stream);
+    const int hq = (int)n_q_heads;
+    auto go = [&](auto s_tag, auto p_tag, auto q_tag) {
+        using S = decltype(s_tag);
+        using P = decltype(p_tag);
+        using QO = decltype(q_tag);
+        kv_append_rope_kernel<S, P, QO><<<grid, 256, 0, st>>>(
+            static_cast<P*>(pool->k), static_cast<P*>(pool->v), geom_of(pool), layer,
+            static_cast<const S*>(k_new), static_cast<const S*>(v_new), slot_mapping, positions,
+            n_tokens, cos_table, sin_table, table_rows, interleaved ? 1 : 0,
+            static_cast<const S*>(q), hq, static_cast<QO*>(q_out));
+        return check_launch("kv_append_rope_kernel");
+    };
+    auto with_q = [&](auto s_tag, auto p_tag) {
+        return q_out_dtype == CX_BF16 ? go(s_tag, p_tag, __nv_bfloat16{}) : go(s_tag, p_tag, 0.f);
+    };
+    auto with_p = [&](auto s_tag) {
+        switch (pool->dtype) {
+            case CX_F32: return with_q(s_tag, 0.f);
+            case CX_BF16: return with_q(s_tag, __nv_bfloat16{});
+            case CX_F16: return with_q(s_tag, __half{});
+            default: return fail(CX_ERR_DTYPE, "cx_kv_append_rope: unknown pool dtype");
+        }
+    };
+    return src_dtype == CX_BF16 ? with_p(__nv_bfloat16{}) : with_p(0.f);
 }
 
 int cx_kv_gather(const cx_pool* pool, int64_t layer, const int32_t* block_table,

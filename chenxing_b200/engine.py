@@ -65,6 +65,8 @@ class StepPlan:
     cow: tuple | None                  # (src, dst, n_valid) int32 device tensors
     cow_host: list                     # [(src, dst, n_valid)]
     appended: set = field(default_factory=set)
+    positions: torch.Tensor | None = None   # (sum q_lens,) absolute positions, built lazily
+    cow_done: bool = False
 
     @property
     def n_rows(self) -> int:
@@ -274,6 +276,28 @@ class BatchedKVEngine:
         the plan's copy-on-write copies of that layer fused in."""
         self.cache.append_batch(layer, k, v, plan.slots, cow=plan.cow)
         plan.appended.add(int(layer))
+
+    def append_rope(self, plan: StepPlan, layer: int, k, v, rope, q=None,
+                    q_out_dtype=torch.bfloat16):
+        """``append`` with RoPE fused in: K rotated at each token's absolute
+        position (its sequence's committed length + index in the step), V
+        copied, and Q rotated into the returned tensor (transformer.py:84-87).
+        The plan's copy-on-write copies run once, for every layer, before the
+        first such call."""
+        if plan.cow_host and not plan.cow_done:
+            for src, dst, n in plan.cow_host:          # all layers at once
+                if n > 0:
+                    self.cache.copy_blocks([src], [dst], n)
+            plan.cow_done = True
+        if plan.positions is None:
+            pos = np.concatenate([np.arange(n0, n0 + n, dtype=np.int64)
+                                  for n0, n in zip(plan.n_past, plan.q_lens)]) \
+                if len(plan.q_lens) else np.zeros(0, dtype=np.int64)
+            plan.positions = torch.from_numpy(pos).to(self.cache.device)
+        qo = self.cache.append_rope(layer, k, v, plan.slots, plan.positions, rope, q,
+                                    q_out_dtype)
+        plan.appended.add(int(layer))
+        return qo
 
     def attend(self, plan: StepPlan, layer: int, q, out=None):
         """Paged attention of the step's query rows (sum q_lens, Hq, D) over

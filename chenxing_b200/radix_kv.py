@@ -8,6 +8,8 @@ bit-exact; the K/V pools are CUDA tensors and every data movement is a
 libcxkv kernel:
 
 * ``write_layer``  -> ``cx_kv_append``  (slot-mapped scatter, radix_kv.py:113-128)
+* ``append_rope``  -> ``cx_kv_append_rope`` (apply_rope on Q and K fused into the
+  scatter, transformer.py:84-87)
 * ``read_layer``   -> ``cx_kv_gather``  (radix_kv.py:130-144)
 * ``copy_blocks`` / ``cow_tail`` / ``compact`` -> ``cx_block_copy`` (no reference
   counterpart)
@@ -434,6 +436,43 @@ class RadixPagedKVCache(RadixIndex):
         if cow is not None:
             cow = tuple(to_device(c, self.device, float_only=False).to(torch.int32) for c in cow)
         self.append_slots(layer, kt, vt, st, cow)
+
+    def append_rope(self, layer: int, k, v, slot_mapping, positions, rope, q=None,
+                    q_out_dtype=torch.bfloat16):
+        """Rotate K with RoPE while appending it (``apply_rope`` then
+        ``write_layer``, transformer.py:84-87), copy V, and return Q rotated
+        into a new (T, Hq, D) tensor of ``q_out_dtype`` (None without q).
+        k, v: (T, Hkv, D) float32 or bf16; positions: (T,) absolute token
+        positions; rope: a ``chenxing_b200.rope.RopeTables``."""
+        kt = to_device(k, self.device)
+        vt = to_device(v, self.device)
+        if kt.dtype not in (torch.float32, torch.bfloat16) or vt.dtype != kt.dtype:
+            raise TypeError("k and v must both be float32 or both bfloat16")
+        T = int(kt.shape[0])
+        shape = (T, self.n_kv_heads, self.head_dim)
+        if tuple(kt.shape) != shape or tuple(vt.shape) != shape:
+            raise ValueError(f"k/v must have shape {shape}")
+        if rope.head_dim != self.head_dim:
+            raise ValueError("RoPE tables were built for another head_dim")
+        st = to_device(slot_mapping, self.device, float_only=False).to(torch.int64)
+        ps = to_device(positions, self.device, float_only=False).to(torch.int64)
+        if st.numel() != T or ps.numel() != T:
+            raise ValueError("slot_mapping and positions need one entry per token")
+        qt = qo = None
+        hq = 0
+        if q is not None:
+            qt = to_device(q, self.device).to(kt.dtype).contiguous()
+            if qt.dim() != 3 or qt.shape[0] != T or qt.shape[2] != self.head_dim:
+                raise ValueError("q must be (T, Hq, head_dim)")
+            hq = int(qt.shape[1])
+            qo = torch.empty(tuple(qt.shape), dtype=q_out_dtype, device=self.device)
+        _lib.check(_lib.lib().cx_kv_append_rope(
+            self._pool, int(layer), kt.contiguous().data_ptr(), vt.contiguous().data_ptr(),
+            _lib.cx_dtype(kt.dtype), st.data_ptr(), ps.data_ptr(), T, rope.cos.data_ptr(),
+            rope.sin.data_ptr(), rope.rows, int(rope.interleaved), _lib.ptr(qt), hq,
+            _lib.ptr(qo), _lib.cx_dtype(q_out_dtype), _lib.stream_ptr(self.device)),
+            "cx_kv_append_rope")
+        return qo
 
     def decode_batch(self, layer: int, q, batch, out=None, replan=None):
         """Paged flash-decode of one query token per sequence of ``batch``."""

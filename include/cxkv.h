@@ -49,7 +49,8 @@ enum {
     CX_DEV_BAD_BLOCK = 1u << 1,    /* block id outside [0, n_blocks)          */
     CX_DEV_TABLE_OVERRUN = 1u << 2,/* context longer than its block table     */
     CX_DEV_WAIT_TIMEOUT = 1u << 3, /* a bounded pipeline wait gave up         */
-    CX_DEV_BAD_QLEN = 1u << 4      /* query length > context or > max_q_len   */
+    CX_DEV_BAD_QLEN = 1u << 4,     /* query length > context or > max_q_len   */
+    CX_DEV_BAD_POSITION = 1u << 5  /* RoPE position outside the cos/sin table */
 };
 
 /* A block pool: K and V device buffers plus their shape. */
@@ -104,6 +105,26 @@ int cx_kv_append(const cx_pool* pool, int64_t layer,
                  const int64_t* slot_mapping, int64_t n_tokens,
                  const int32_t* cow_src, const int32_t* cow_dst,
                  const int32_t* cow_n_valid, int64_t n_cow, void* stream);
+
+/* RoPE fused into the KV append — replaces apply_rope on Q and K followed by
+ * write_layer (chenxing/model/transformer.py:84-87, chenxing/core/tensor.py:
+ * 129-180, radix_kv.py:113-128).  Token t sits at absolute position
+ * positions[t] (0 <= position < table_rows); cos_table / sin_table are the
+ * float32 [table_rows][head_dim] tables of build_rope_cache
+ * (tensor.py:80-121).  K rows are rotated and scattered like cx_kv_append
+ * (negative slot = skip, no copy-on-write), V rows are copied, and when
+ * n_q_heads > 0 the Q rows q [n_tokens][n_q_heads][head_dim] (src_dtype) are
+ * rotated into q_out (q_out_dtype CX_F32 or CX_BF16).  interleaved != 0 pairs
+ * elements (2j, 2j+1), else (j, j + head_dim/2).  Each rotated element is the
+ * fp32 expression the reference evaluates (two products, one sum, no fused
+ * multiply-add), then rounded to the destination type.  head_dim must be
+ * even; a position outside the table raises CX_DEV_BAD_POSITION and skips
+ * the token. */
+int cx_kv_append_rope(const cx_pool* pool, int64_t layer, const void* k_new, const void* v_new,
+                      int32_t src_dtype, const int64_t* slot_mapping, const int64_t* positions,
+                      int64_t n_tokens, const float* cos_table, const float* sin_table,
+                      int64_t table_rows, int32_t interleaved, const void* q,
+                      int64_t n_q_heads, void* q_out, int32_t q_out_dtype, void* stream);
 
 /* KV gather — replaces RadixPagedKVCache.read_layer
  * (chenxing/engine/radix_kv.py:130-144): k_out/v_out [n_tokens][n_kv_heads]

@@ -20,6 +20,13 @@ Writes:
   engine_meta.json block-table growth (LLMEngine._ensure_capacity), speculative
                   rollback (SpeculativeDecoder._sync_to) and the slot each
                   written token landed in, observed from the reference pool.
+  rope.npz        reference build_rope_cache tables (plain and YaRN-scaled) and
+                  apply_rope outputs (half-split and interleaved layouts, token
+                  positions picked from the table) on seeded inputs.
+
+    python tests/golden/make_golden.py --reference <path> --only rope
+
+regenerates rope.npz alone.
 """
 from __future__ import annotations
 
@@ -274,10 +281,46 @@ def engine_meta(ref_radix, LLMEngine, seed=9):
     return {"block_size": bs, "n_blocks": 256, "n_seqs": len(seqs), "trace": trace}
 
 
+ROPE_CASES = [
+    # name, table rows, head_dim, base, scaling_factor, original_max_pos, interleaved
+    ("plain_hs", 8192, 128, 10000.0, 1.0, 4096, False),
+    ("plain_il", 8192, 128, 10000.0, 1.0, 4096, True),
+    ("llama3_hs", 8192, 128, 500000.0, 1.0, 4096, False),
+    ("yarn_hs", 2048, 64, 10000.0, 4.0, 512, False),
+    ("yarn_il", 2048, 64, 10000.0, 4.0, 512, True),
+]
+
+
+def rope_goldens(build_rope_cache, apply_rope, seed=21):
+    """Per ROPE_CASES entry: the table rows the case uses, a digest of the
+    whole cos / sin tables, seeded (T, H, D) inputs and apply_rope's output."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for name, rows, d, base, scale, omax, il in ROPE_CASES:
+        cos, sin = build_rope_cache(rows, d, base, scaling_factor=scale,
+                                    original_max_pos=omax, dtype=np.float32)
+        x = rng.standard_normal((17, 3, d)).astype(np.float32)
+        pos = rng.integers(0, rows, size=17).astype(np.int64)
+        pos[:3] = [0, 1, rows - 1]
+        out[name + "_table_digest"] = np.frombuffer(digest(cos, sin).encode(), dtype=np.uint8)
+        out[name + "_cos_rows"], out[name + "_sin_rows"] = cos[pos], sin[pos]
+        out[name + "_x"], out[name + "_pos"] = x, pos
+        out[name + "_out"] = apply_rope(x, cos, sin, positions=pos, interleaved=il)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to a Chenxing checkout")
+    ap.add_argument("--only", choices=["rope"], default=None)
     args = ap.parse_args()
+    if args.only == "rope":
+        sys.path.insert(0, args.reference)
+        from chenxing.core.tensor import apply_rope, build_rope_cache
+        np.savez_compressed(os.path.join(HERE, "rope.npz"),
+                            **rope_goldens(build_rope_cache, apply_rope))
+        print("rope.npz written to", HERE)
+        return
     sys.path.insert(0, args.reference)
     sys.path.insert(0, ROOT)
     import ml_dtypes
@@ -302,6 +345,9 @@ def main():
         json.dump(radix_script(ref_radix), f)
     with open(os.path.join(HERE, "engine_meta.json"), "w") as f:
         json.dump(engine_meta(ref_radix, LLMEngine), f)
+    from chenxing.core.tensor import apply_rope, build_rope_cache
+    np.savez_compressed(os.path.join(HERE, "rope.npz"),
+                        **rope_goldens(build_rope_cache, apply_rope))
     print("golden fixtures written to", HERE)
 
 

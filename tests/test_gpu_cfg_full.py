@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_cases import (BF16_RTOL, assert_close_rows, claim_blocks, oracle_rows,
+from gpu_cases import (BF16_RTOL, assert_close_rows, bf16_round, claim_blocks, oracle_rows,
                        pool_rows)
 
 pytestmark = pytest.mark.gpu
@@ -450,3 +450,45 @@ def test_engine_shared_tail_verify_rollback():
     assert eng.seqs[1].n_tokens == 38
     step([2, 5])
     assert eng.seqs[1].n_tokens == 43
+
+
+def test_engine_append_rope_then_verify_matches_oracle():
+    """BatchedKVEngine.append_rope positions each token at its sequence's
+    committed length + index (transformer.py:84-87 with positions =
+    n_past + arange(T)); Q and K rotated, then verify attention."""
+    from chenxing_b200 import RadixPagedKVCache, RopeTables
+    from chenxing_b200.engine import BatchedKVEngine
+    from oracle.rope import rotate
+
+    cache = RadixPagedKVCache(64, BS, 1, HK, D, dtype="bfloat16", host_io=False)
+    eng = BatchedKVEngine(cache, n_q_heads=HQ)
+    rope = RopeTables(4096, D, 500000.0)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(12)
+    rng = np.random.default_rng(12)
+    prompts = [[int(x) for x in rng.integers(0, 1000, size=n)] for n in (70, 33)]
+    hist = {}
+    for sid, pr in enumerate(prompts):
+        eng.add(sid, pr)
+    for step_q in ([70, 33], [5, 9]):
+        p = eng.plan([0, 1], step_q)
+        rows = sum(step_q)
+        k, v = _randn((rows, HK, D), g, 1.0), _randn((rows, HK, D), g, 1.0)
+        q = _randn((rows, HQ, D), g, 1.0)
+        qr = eng.append_rope(p, 0, k, v, rope, q=q)
+        out = eng.attend(p, 0, qr).cpu().numpy()
+        cos, sin = rope.cos.cpu().numpy(), rope.sin.cpu().numpy()
+        o = 0
+        for sid, (n0, ql) in enumerate(zip(p.n_past, step_q)):
+            pos = np.arange(n0, n0 + ql)
+            kr = bf16_round(rotate(k[o:o + ql].float().cpu().numpy(), cos, sin, pos))
+            hist[sid] = np.concatenate([hist.get(sid, np.zeros((0, HK, D), np.float32)), kr])
+            vv = np.concatenate([hist.get(("v", sid), np.zeros((0, HK, D), np.float32)),
+                                 v[o:o + ql].float().cpu().numpy()])
+            hist[("v", sid)] = vv
+            qref = bf16_round(rotate(q[o:o + ql].float().cpu().numpy(), cos, sin, pos))
+            assert np.array_equal(qr[o:o + ql].float().cpu().numpy(), qref)
+            ref = oracle_rows(qref, hist[sid], vv)
+            assert_close_rows(out[o:o + ql], ref, BF16_RTOL, f"seq {sid}")
+            o += ql
+        eng.commit(p)

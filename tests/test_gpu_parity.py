@@ -397,3 +397,66 @@ def test_cfg2_full_size_properties():
     case.cache.append_batch(0, case.k, ones, slots)
     out3 = case.run()
     assert np.abs(out3 - 0.375).max() <= 2e-3
+
+
+# ---------------------------------------------------------------------------
+# RoPE fused into the KV append (cx_kv_append_rope) against the reference's
+# apply_rope goldens: bit-exact for fp32 pools / outputs, bf16 = RNE of them
+# ---------------------------------------------------------------------------
+def _rope_case(name):
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    from make_golden import ROPE_CASES
+    from chenxing_b200 import RopeTables
+    row = [c for c in ROPE_CASES if c[0] == name][0]
+    _, rows, d, base, scale, omax, il = row
+    g = np.load(os.path.join(GOLDEN, "rope.npz"))
+    rope = RopeTables(rows, d, base, scaling_factor=scale, original_max_pos=omax, interleaved=il)
+    return g[name + "_x"], g[name + "_pos"], g[name + "_out"], rope
+
+
+@pytest.mark.parametrize("name", ["plain_hs", "plain_il", "llama3_hs", "yarn_hs", "yarn_il"])
+@pytest.mark.parametrize("pool_dtype", [np.float32, "bfloat16"])
+def test_append_rope_matches_reference_apply_rope(name, pool_dtype):
+    from chenxing_b200 import RadixPagedKVCache
+    x, pos, want, rope = _rope_case(name)
+    T, H, D = x.shape
+    c = RadixPagedKVCache(8, 16, 2, H, D, dtype=pool_dtype, host_io=False)
+    rng = np.random.default_rng(1)
+    v = rng.standard_normal(x.shape).astype(np.float32)
+    slots = np.arange(T, dtype=np.int64) + 37           # blocks 2.. of the pool
+    slots[5] = -1                                      # padding token: skipped
+    q_out = c.append_rope(1, x, v, slots, pos, rope, q=x, q_out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert np.array_equal(q_out.cpu().numpy(), want)  # Q rotated, fp32, bit-exact
+    k_pool = c.k_pool[1].reshape(-1, H, D).float().cpu().numpy()
+    v_pool = c.v_pool[1].reshape(-1, H, D).float().cpu().numpy()
+    keep = slots >= 0
+    exp_k, exp_v = want[keep], v[keep]
+    if pool_dtype == "bfloat16":
+        exp_k, exp_v = bf16_round(exp_k), bf16_round(exp_v)
+    assert np.array_equal(k_pool[slots[keep]], exp_k)
+    assert np.array_equal(v_pool[slots[keep]], exp_v)
+    assert not k_pool[slots[5] if slots[5] >= 0 else 37 + 5].any()   # untouched slot
+    assert not c.k_pool[0].float().abs().sum().item()                 # other layer untouched
+    q_bf = c.append_rope(1, x, v, slots, pos, rope, q=x, q_out_dtype=torch.bfloat16)
+    assert np.array_equal(q_bf.float().cpu().numpy(), bf16_round(want))
+
+
+def test_append_rope_bf16_source_and_bad_position_flag():
+    from chenxing_b200 import RadixPagedKVCache, _lib
+    x, pos, want, rope = _rope_case("plain_hs")
+    T, H, D = x.shape
+    c = RadixPagedKVCache(4, 16, 1, H, D, dtype="bfloat16", host_io=False)
+    xb = torch.from_numpy(x).bfloat16().cuda()
+    slots = torch.arange(T, dtype=torch.int64, device="cuda")
+    c.append_rope(0, xb, xb, slots, pos, rope)
+    from oracle.rope import rotate
+    cos, sin = rope.cos.cpu().numpy(), rope.sin.cpu().numpy()
+    ref = bf16_round(rotate(xb.float().cpu().numpy(), cos, sin, pos, False))
+    got = c.k_pool[0].reshape(-1, H, D)[:T].float().cpu().numpy()
+    assert np.array_equal(got, ref)
+    bad = pos.copy()
+    bad[3] = rope.rows                                  # one past the table
+    c.append_rope(0, xb, xb, slots, bad, rope)
+    assert _lib.device_flags(clear=True) & 32
