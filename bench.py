@@ -273,6 +273,43 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+class AllGatherer:
+    """NCCL all-gather of each step's attention rows on a side stream."""
+
+    def __init__(self, dist, dev, world, gathered, shape):
+        import torch
+        self.dist, self.gathered = dist, gathered
+        self.comm = torch.cuda.Stream(dev)
+        self.src = [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(2)]
+        self.freed = [torch.cuda.Event() for _ in range(2)]
+        self.ready = [torch.cuda.Event() for _ in range(2)]
+        self.k = 0
+        self.times = []
+
+    def issue(self, stream, rows):
+        import torch
+        j = self.k & 1
+        self.k += 1
+        stream.wait_event(self.freed[j])          # gather of two steps ago is done
+        self.src[j].copy_(rows)
+        self.ready[j].record(stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(self.comm):
+            self.comm.wait_event(self.ready[j])
+            e0.record(self.comm)
+            self.dist.all_gather_into_tensor(self.gathered, self.src[j])
+            e1.record(self.comm)
+            self.freed[j].record(self.comm)
+        self.times.append((e0, e1))
+
+    def reset_timing(self):
+        self.times = []
+
+    def mean_ms(self):
+        if not self.times:
+            return None
+        return float(np.mean([a.elapsed_time(b) for a, b in self.times]))
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -330,6 +367,10 @@ def run_ours(args):
     stream = torch.cuda.Stream(dev)
     sp = stream.cuda_stream
     launches = [0]
+    # The per-step all-gather of the last layer's rows runs on its own stream,
+    # overlapped with the next step and timed by its own events; it reads a
+    # double-buffered copy so the next step never overwrites rows in flight.
+    ag = AllGatherer(dist, dev, world, gathered, (BATCH, HQ, D)) if world > 1 else None
 
     def one_step(s, ev=None):
         bt = batches[s]
@@ -348,8 +389,8 @@ def run_ours(args):
             if ev is not None:
                 ev[l][1].record(stream)
             launches[0] += 2 + (l == 0)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, outs[layers - 1])
+        if ag is not None:
+            ag.issue(stream, outs[layers - 1])
 
     def barrier():
         if world > 1:
@@ -376,8 +417,12 @@ def run_ours(args):
         barrier()
         torch.cuda.synchronize(dev)
         start.record(stream)
+        if ag is not None:
+            ag.reset_timing()
         for i in range(args.steps):
             one_step(args.warmup + i, evs.get(i))
+        if ag is not None:
+            stream.wait_stream(ag.comm)             # the timed region includes the gathers
         end.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
@@ -389,6 +434,7 @@ def run_ours(args):
     if flags:
         raise RuntimeError(f"device flags during timing: {_lib.describe_flags(flags)}")
 
+    ag_ms = ag.mean_ms() if ag is not None else None
     units = sum(units_step[args.warmup:])
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     u = torch.tensor([units], dtype=torch.float64, device=dev)
@@ -444,6 +490,7 @@ def run_ours(args):
                 "config": workload_config(args, world, n_blocks, layers),
                 "hbm_gbs_step": step_gbs, "hbm_frac_step": step_gbs / peak,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "allgather_ms_per_step": ag_ms,
                 "gpu_launches": timed_launches, "clocks": clocks}
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -478,6 +525,7 @@ def run_e2e(args, lib, pool, cache, batches, slots, layers, n_sets, dev, world, 
     sp = main.cuda_stream
     gathered = torch.empty((world * BATCH, HQ, D), dtype=torch.float32, device=dev) \
         if world > 1 else None
+    ag = AllGatherer(dist, dev, world, gathered, (BATCH, HQ, D)) if world > 1 else None
     # per-step scheduler metadata also comes from the host: context lengths
     # (for the plan) and the append slots
     hctx = [b.ctx_lens.cpu().pin_memory() for b in batches]
@@ -521,9 +569,9 @@ def run_e2e(args, lib, pool, cache, batches, slots, layers, n_sets, dev, world, 
                 copy_out.wait_event(done_ev[l])
                 hout[l].copy_(dout[j], non_blocking=True)
                 out_ev[l].record(copy_out)
-        if world > 1:
+        if ag is not None:
             with torch.cuda.stream(main):
-                dist.all_gather_into_tensor(gathered, dout[(layers - 1) & 1])
+                ag.issue(main, dout[(layers - 1) & 1])
         main.wait_stream(copy_out)
 
     for s in range(args.warmup):
@@ -536,6 +584,8 @@ def run_e2e(args, lib, pool, cache, batches, slots, layers, n_sets, dev, world, 
     start.record(main)
     for i in range(args.steps):
         step(args.warmup + i)
+    if ag is not None:
+        main.wait_stream(ag.comm)
     end.record(main)
     torch.cuda.synchronize(dev)
     ms = start.elapsed_time(end)
