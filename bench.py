@@ -45,12 +45,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["cfg2", "small", "prefill", "prefill-small", "append"],
+    ap.add_argument("--config", choices=["cfg2", "small", "prefill", "prefill-small", "append",
+                                         "cfg4"],
                     default="cfg2",
                     help="small: 1 layer, pool sized to need (~2 GB, for profiler captures); "
                          "prefill: chunked-prefill attention on the tcgen05 kernel (its own "
                          "JSON line, TFLOP/s); prefill-small: the same, 2 sequences; "
-                         "append: prefill-sized KV append (its own JSON line, GB/s)")
+                         "append: prefill-sized KV append (its own JSON line, GB/s); "
+                         "cfg4: speculative verify, gamma 4 and 8 (their own JSON lines)")
     ap.add_argument("--pool-frac", type=float, default=0.9)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -747,6 +749,102 @@ def run_append(args):
                      "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg}}), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# cfg4: speculative verify (separate mode, not the headline)
+# ---------------------------------------------------------------------------
+def run_verify(args):
+    """cfg4: 128 sequences, ctx ~ U[2048, 16384], gamma + 1 query tokens each
+    (causal within the draft), 4096-token sliding window, Hq 32 / Hkv 8,
+    D 128, bf16.  One step = for each of 4 layers: append the gamma + 1 K/V
+    rows per sequence, then verify attention.  Units = windowed keys
+    attended (min(ctx + gamma + 1, 4096 + gamma) per sequence and layer)."""
+    import torch
+    from chenxing_b200 import PagedBatch, RadixPagedKVCache, _lib
+    from chenxing_b200.batch import slot_mapping
+    from chenxing_b200.workloads import verify_meta
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, W, layers = 128, 4096, 4
+    peak, kind = measured_peak()
+    for gamma in (4, 8):
+        T = gamma + 1
+        ctx = np.random.default_rng(args.seed).integers(2048, 16385, size=B)
+        n_blocks = int(sum(-(-(int(c) + T) // BS) for c in ctx)) + 64
+        wl = verify_meta(n_blocks, seed=args.seed, batch=B, gamma=gamma, window=W,
+                         n_layers=layers)
+        cache = RadixPagedKVCache(n_blocks, BS, layers, HK, D, dtype="bfloat16", device=dev,
+                                  host_io=False)
+        g = torch.Generator(device=dev)
+        g.manual_seed(args.seed)
+        for t in (cache._k, cache._v):
+            for l in range(layers):
+                t[l].normal_(0.0, 1.0 / math.sqrt(D), generator=g)
+        sc = 1.0 / math.sqrt(D)
+        q = (torch.randn((layers, B * T, HQ, D), device=dev, generator=g) * sc).bfloat16()
+        kn = (torch.randn((layers, B * T, HK, D), device=dev, generator=g) * sc).bfloat16()
+        out = torch.empty((B * T, HQ, D), dtype=torch.float32, device=dev)
+        slots = torch.from_numpy(slot_mapping(wl.block_tables, wl.ctx_lens, [T] * B, BS)).to(dev)
+        batch = PagedBatch(cache, wl.block_tables, wl.ctx_lens + T, n_q_heads=HQ,
+                           q_lens=[T] * B, window=W)
+        kind_k = batch.kernel_kind(q.dtype)
+        units = batch.kv_tokens * layers
+        lib, pool = _lib.lib(), cache.cx_pool()
+        stream = torch.cuda.current_stream(dev)
+        sp = stream.cuda_stream
+        c = batch.c_struct()
+        ws, wsn = batch.workspace.data_ptr(), batch.workspace.numel()
+        dec_ev = []
+
+        def step(timed):
+            for l in range(layers):
+                _lib.check(lib.cx_kv_append(pool, l, kn[l].data_ptr(), kn[l].data_ptr(),
+                                            _lib.CX_BF16, slots.data_ptr(), B * T, None, None,
+                                            None, 0, sp), "cx_kv_append")
+                e0 = e1 = None
+                if timed:
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+                        enable_timing=True)
+                    e0.record(stream)
+                _lib.check(lib.cx_paged_verify(pool, l, c, q[l].data_ptr(), _lib.CX_BF16,
+                                               out.data_ptr(), ws, wsn, int(l == 0), sp),
+                           "cx_paged_verify")
+                if timed:
+                    e1.record(stream)
+                    dec_ev.append((e0, e1))
+        for _ in range(args.warmup):
+            step(False)
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            step(True)
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+        if _lib.device_flags(clear=True):
+            raise RuntimeError("device flags raised during the verify bench")
+        ms = start.elapsed_time(end) / args.steps
+        vms = float(np.mean([a.elapsed_time(b) for a, b in dec_ev]))
+        alg = batch.kv_tokens * UNIT_BYTES + B * T * HQ * D * (ELEM + 4) + \
+            4 * sum(len(t) for t in wl.block_tables)
+        gbs = alg / (vms / 1e3) / 1e9
+        print(json.dumps({
+            "metric": f"speculative-verify KV tokens/s (windowed key-layers/s, cfg4 gamma={gamma})",
+            "value": units / (ms / 1e3), "unit": "KV-token-layers/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"cfg4: {B} seqs, ctx U[2048,16384], gamma {gamma}, window "
+                                   f"{W}, {layers} layers per step (append + verify)",
+                       "kernel": kind_k, "rows_per_kv_head": T * (HQ // HK)},
+            "roofline": {"bound": "hbm", "kernel": "paged_attn_mma_kernel (verify)",
+                         "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "peak_source": kind, "algorithmic_bytes_per_launch": alg,
+                         "avg_launch_ms": vms}}), flush=True)
+        del cache, q, kn, out
+        torch.cuda.empty_cache()
+
+
 def main():
     args = parse()
     if args.warmup < 3:
@@ -757,6 +855,8 @@ def main():
         run_prefill(args)
     elif args.config == "append":
         run_append(args)
+    elif args.config == "cfg4":
+        run_verify(args)
     else:
         run_ours(args)
 
