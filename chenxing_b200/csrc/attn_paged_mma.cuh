@@ -618,6 +618,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
 }  // namespace cx
 
 #include "attn_prefill_tc.cuh"
+#include "attn_prefill_tc128.cuh"
 
 namespace cx {
 
@@ -768,7 +769,9 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
         t.hq = (int)b.n_q_heads;
         t.group = G;
         t.tpt = kTcRows / G;
-        t.n_ctiles = (int)((max_q + 2 * t.tpt - 1) / (2 * t.tpt));
+        // head_dim 128: one query tile per CTA; 64: two
+        const int tiles_per_cta = pool->head_dim == 128 ? 1 : 2;
+        t.n_ctiles = (int)((max_q + tiles_per_cta * t.tpt - 1) / (tiles_per_cta * t.tpt));
         t.n_blocks = (int)pool->n_blocks;
         t.layer = (int)layer;
         t.window = b.window > 0 ? (int)(b.window < (1ll << 30) ? b.window : (1ll << 30)) : 0;
@@ -784,8 +787,8 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
         rc = make_pool_tmap(&tv, pool->v, pool, 1);
         if (rc) return rc;
         if (pool->head_dim == 128)
-            return q_dtype == CX_F32 ? launch_tc<128, float>(tk, tv, t, st)
-                                     : launch_tc<128, __nv_bfloat16>(tk, tv, t, st);
+            return q_dtype == CX_F32 ? launch_tc128<float>(tk, tv, t, st)
+                                     : launch_tc128<__nv_bfloat16>(tk, tv, t, st);
         return q_dtype == CX_F32 ? launch_tc<64, float>(tk, tv, t, st)
                                  : launch_tc<64, __nv_bfloat16>(tk, tv, t, st);
     }

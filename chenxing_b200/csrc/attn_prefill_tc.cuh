@@ -8,8 +8,11 @@
 // M = 128 operand even for GQA.  Keys are walked in tiles of kTcKeys = 64
 // (four 16-token pool blocks):
 //
-//   producer warp  : TMA loads of the four blocks' K and V tiles (128-byte
-//                    column halves, 128-byte swizzle) into a 4-stage ring;
+//   producer warps : TMA loads of the four blocks' K and V tiles (128-byte
+//                    column halves, 128-byte swizzle) into a 4-stage ring,
+//                    issued from three warps (one TMA instruction costs its
+//                    issuing thread ~100 cycles, so one thread alone cannot
+//                    keep up with the tensor pipe);
 //   MMA warp       : one thread issues tcgen05.mma (kind::f16, bf16 x bf16 ->
 //                    fp32) S_w = Q_w K^T into TMEM and O_w += P_w V into TMEM
 //                    for both query tiles w = 0, 1: the next tile's scores
@@ -71,10 +74,34 @@ struct TcCfg {
     // TMEM columns: S_0 [0, 64), S_1 [64, 128), O_0 [128, 128 + D),
     // O_1 [256, 256 + D); all 512 are taken (one CTA per SM by shared memory)
     static constexpr int TMEM_COLS = 512;
-    static constexpr int THREADS = 320;                      // 2 x 4 softmax, producer, MMA
-    static constexpr int PRODUCER_WARP = 8;
-    static constexpr int MMA_WARP = 9;
+    static constexpr int N_PRODUCERS = 3;
+    static constexpr int THREADS = 384;                      // 2 x 4 softmax, 3 producers, MMA
+    static constexpr int PRODUCER_WARP = 8;                  // first producer warp
+    static constexpr int MMA_WARP = 11;
 };
+
+// AND of `pred` over the `nthreads` threads that meet at named barrier `id`.
+__device__ __forceinline__ bool bar_red_and(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %3, 0;\n\t"
+        "bar.red.and.pred p, %1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(id), "r"(nthreads), "r"((uint32_t)pred)
+        : "memory");
+    return r != 0;
+}
+
+// 2^x as one special-function-unit instruction (ex2.approx.ftz: relative error
+// about 2^-22, far below the bf16 rounding of P; 2^-inf = +0 and results below
+// the normal range flush to 0, which is what masked keys need).
+__device__ __forceinline__ float ex2_sfu(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // ---- tcgen05 helpers ------------------------------------------------------
 // Shared-memory matrix descriptor (tcgen05 format): start address, leading
@@ -226,7 +253,7 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
 
     if (tid == 0) {
         for (int s = 0; s < kTcStages; ++s) {
-            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_full[s], C::N_PRODUCERS);
             mbar_init(&kv_empty[s], 1);
         }
         for (int w = 0; w < 2; ++w) {
@@ -247,7 +274,13 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    // Q tiles -> shared memory (bf16, swizzled K-major); rows past the chunk are zero
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+    // Q tiles -> shared memory (bf16, swizzled K-major; rows past the chunk are
+    // zero), 16-byte loads all in flight at once.  Only the MMA warp waits for
+    // them (named barrier 3): the producers start loading K and V at once.
     if (warp < 8) {
         const int w = warp >> 2, r = tid & 127;
         const int t = t0 + w * tpt + r / G;
@@ -255,65 +288,97 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
         const bool ok = t < t_end;
         const QT* src = static_cast<const QT*>(p.q) + ((int64_t)(qs + t) * p.hq + head) * D;
         unsigned char* qdst = sq + w * C::Q_BYTES;
-#pragma unroll 4
-        for (int c = 0; c < D / 8; ++c) {
-            uint32_t wv[4] = {0u, 0u, 0u, 0u};
-            if (ok) {
+        const bool vec = (reinterpret_cast<uintptr_t>(p.q) & 15) == 0;
+        constexpr int EPV = 16 / (int)sizeof(QT);            // elements per 16-byte vector
+        uint4 raw[D * (int)sizeof(QT) / 16];
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    wv[e] = pack_bf16(Conv<QT>::to_f(src[c * 8 + 2 * e]),
-                                      Conv<QT>::to_f(src[c * 8 + 2 * e + 1]));
+        for (int v = 0; v < D * (int)sizeof(QT) / 16; ++v) {
+            if (!ok) {
+                raw[v] = make_uint4(0, 0, 0, 0);
+            } else if (vec) {
+                raw[v] = __ldg(reinterpret_cast<const uint4*>(src) + v);
+            } else {
+                QT e[EPV];
+#pragma unroll
+                for (int k = 0; k < EPV; ++k) e[k] = src[v * EPV + k];
+                memcpy(&raw[v], e, 16);
             }
-            *reinterpret_cast<uint4*>(qdst + tc_swz(r, c * 8, kTcRows)) =
-                make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        }
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {                      // 8 dims per 16-byte chunk
+            uint4 w4;
+            if constexpr (sizeof(QT) == 2) {
+                w4 = raw[c];
+            } else {
+                const uint4 a0 = raw[2 * c], a1 = raw[2 * c + 1];
+                w4 = make_uint4(pack_bf16(__uint_as_float(a0.x), __uint_as_float(a0.y)),
+                                pack_bf16(__uint_as_float(a0.z), __uint_as_float(a0.w)),
+                                pack_bf16(__uint_as_float(a1.x), __uint_as_float(a1.y)),
+                                pack_bf16(__uint_as_float(a1.z), __uint_as_float(a1.w)));
+            }
+            *reinterpret_cast<uint4*>(qdst + tc_swz(r, c * 8, kTcRows)) = w4;
         }
         fence_async_smem();
+        named_bar_arrive(3, 256 + 32);
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *s_tmem;
 
-    if (warp == C::PRODUCER_WARP) {
-        // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            const int32_t* tab = p.tables + (int64_t)b * p.table_stride;
-            const int first_id = kb0 < nblk_seq ? tab[kb0] : 0;
-            for (int i = 0; i < n_tiles; ++i) {
-                const int s = i % kTcStages;
-                const int use = i / kTcStages;
-                if (use > 0 && !mbar_wait_bounded(&kv_empty[s], (use - 1) & 1, s_abort,
-                                                  kWaitLimitNs)) {
+    if (warp >= C::PRODUCER_WARP && warp < C::PRODUCER_WARP + C::N_PRODUCERS) {
+        // ---------------- TMA producers ----------------
+        // Producer pw issues the (block j, K or V) pairs pw, pw + 3, ... of each
+        // stage.  The three warps decide together at a named barrier whether a
+        // stage goes ahead, so a stage is issued by all of them or by none and
+        // `s_issued` stays exact for the teardown drain.
+        const int pw = warp - C::PRODUCER_WARP;
+        constexpr int PAIRS = 2 * (kTcKeys / kBlockTok);       // (block, K or V) per stage
+        constexpr int PAIR_BYTES = kBlockTok * D * 2;
+        int my_pairs = 0;
+        for (int q = pw; q < PAIRS; q += C::N_PRODUCERS) ++my_pairs;
+        const int32_t* tab = p.tables + (int64_t)b * p.table_stride;
+        const int first_id = kb0 < nblk_seq ? tab[kb0] : 0;
+        int ids = 0;                                           // 32 block ids, one per lane
+        for (int i = 0; i < n_tiles; ++i) {
+            const int s = i % kTcStages;
+            const int use = i / kTcStages;
+            if ((i * (kTcKeys / kBlockTok)) % 32 == 0) {
+                const int blk = kb0 + i * (kTcKeys / kBlockTok) + lane;
+                ids = blk < nblk_seq ? tab[blk] : first_id;
+                if (ids < 0 || ids >= p.n_blocks) {
+                    raise_flag(CX_DEV_BAD_BLOCK);
+                    ids = 0;
+                }
+            }
+            bool go = true;
+            if (lane == 0 && use > 0 &&
+                !mbar_wait_bounded(&kv_empty[s], (use - 1) & 1, s_abort, kWaitLimitNs))
+                go = false;
+            go = __shfl_sync(0xffffffffu, go, 0) && !*s_abort;
+            if (!bar_red_and(1, 32 * C::N_PRODUCERS, go)) {
+                if (lane == 0) {
                     *s_abort = 1;
                     raise_flag(CX_DEV_WAIT_TIMEOUT);
-                    break;
                 }
-                if (*s_abort) break;
-                mbar_arrive_expect_tx(&kv_full[s], C::STAGE);
-                unsigned char* kd = skv + s * C::STAGE;
-                unsigned char* vd = kd + C::KT_BYTES;
-#pragma unroll
-                for (int j = 0; j < kTcKeys / kBlockTok; ++j) {
-                    const int blk = kb0 + i * (kTcKeys / kBlockTok) + j;
-                    int id = blk < nblk_seq ? tab[blk] : first_id;
-                    if (id < 0 || id >= p.n_blocks) {
-                        raise_flag(CX_DEV_BAD_BLOCK);
-                        id = 0;
-                    }
-                    const int z = (p.layer * p.n_blocks + id) * p.hk + h;
-#pragma unroll
-                    for (int hf = 0; hf < C::HALVES; ++hf) {
-                        tma_load_3d(kd + hf * C::KV_HALF + j * 2048, &tmk, &kv_full[s],
-                                    hf * 64, 0, z);
-                        tma_load_3d(vd + hf * C::KV_HALF + j * 2048, &tmv, &kv_full[s],
-                                    hf * 64, 0, z);
-                    }
-                }
-                *s_issued = i + 1;
+                break;
             }
+            unsigned char* kd = skv + s * C::STAGE;
+            if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], my_pairs * PAIR_BYTES);
+            for (int q = pw; q < PAIRS; q += C::N_PRODUCERS) {
+                const int j = q >> 1;                          // block of the stage
+                const int id = __shfl_sync(0xffffffffu, ids,
+                                           (i * (kTcKeys / kBlockTok) + j) & 31);
+                if (lane == 0) {
+                    const int z = (p.layer * p.n_blocks + id) * p.hk + h;
+                    unsigned char* dst = kd + (q & 1) * C::KT_BYTES + j * 2048;
+#pragma unroll
+                    for (int hf = 0; hf < C::HALVES; ++hf)
+                        tma_load_3d(dst + hf * C::KV_HALF, (q & 1) ? &tmv : &tmk, &kv_full[s],
+                                    hf * 64, 0, z);
+                }
+            }
+            if (pw == 0 && lane == 0) *s_issued = i + 1;
         }
     } else if (warp == C::MMA_WARP) {
         // ---------------- MMA issuer ----------------
+        named_bar_sync(3, 256 + 32);                   // Q is in shared memory
         if (lane == 0) {
             constexpr uint32_t idesc_s = tc_idesc(kTcRows, kTcKeys, 0);
             constexpr uint32_t idesc_o = tc_idesc(kTcRows, D, 1);
@@ -453,7 +518,7 @@ __global__ void __launch_bounds__(TcCfg<D>::THREADS, 1)
             float sum = 0.f;
 #pragma unroll
             for (int j = 0; j < kTcKeys; ++j) {
-                sv[j] = exp2f(sv[j] - m_use);
+                sv[j] = ex2_sfu(sv[j] - m_use);
                 sum += sv[j];
             }
             l = l * alpha + sum;

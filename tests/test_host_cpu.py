@@ -297,3 +297,4 @@ def test_reference_publish_lets_eviction_free_pinned_blocks(mode):
     idx.evict(1)
     freed = [b for b in pinned if b in idx._free]
     assert bool(freed) == (mode == "reference")
+
