@@ -619,6 +619,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
 
 #include "attn_prefill_tc.cuh"
 #include "attn_prefill_tc128.cuh"
+#include "attn_prefill_tc256.cuh"
 
 namespace cx {
 
@@ -769,8 +770,10 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
         t.hq = (int)b.n_q_heads;
         t.group = G;
         t.tpt = kTcRows / G;
-        // head_dim 128: one query tile per CTA; 64: two
-        const int tiles_per_cta = pool->head_dim == 128 ? 1 : 2;
+        // head_dim 128: one query tile per CTA when no sequence has more than
+        // one (short verify chains), else two; head_dim 64: two
+        const int64_t q_tiles = (max_q + t.tpt - 1) / t.tpt;
+        const int tiles_per_cta = pool->head_dim == 128 && q_tiles == 1 ? 1 : 2;
         t.n_ctiles = (int)((max_q + tiles_per_cta * t.tpt - 1) / (tiles_per_cta * t.tpt));
         t.n_blocks = (int)pool->n_blocks;
         t.layer = (int)layer;
@@ -787,8 +790,11 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
         rc = make_pool_tmap(&tv, pool->v, pool, 1);
         if (rc) return rc;
         if (pool->head_dim == 128)
-            return q_dtype == CX_F32 ? launch_tc128<float>(tk, tv, t, st)
-                                     : launch_tc128<__nv_bfloat16>(tk, tv, t, st);
+            return tiles_per_cta == 1
+                       ? (q_dtype == CX_F32 ? launch_tc128<float>(tk, tv, t, st)
+                                            : launch_tc128<__nv_bfloat16>(tk, tv, t, st))
+                       : (q_dtype == CX_F32 ? launch_tc256<float>(tk, tv, t, st)
+                                            : launch_tc256<__nv_bfloat16>(tk, tv, t, st));
         return q_dtype == CX_F32 ? launch_tc<64, float>(tk, tv, t, st)
                                  : launch_tc<64, __nv_bfloat16>(tk, tv, t, st);
     }

@@ -60,6 +60,74 @@ __device__ __forceinline__ void t128_item(int q, int n, bool& is_v, int& i) {
     }
 }
 
+// TMA producer of the 128-key kernels (run by each of NPROD warps): ring items
+// (32 KB K or V tiles of eight 16-token pool blocks, two 128-byte swizzled
+// column halves each) in the order t128_item gives, key tile i + rot (mod
+// n_tiles) for item tile i.  Producer pw loads blocks pw, pw + NPROD, ... of
+// each item.  The warps decide together at named barrier 1 whether an item goes
+// ahead, so an item is issued by all of them or by none and `s_issued` stays
+// exact for the teardown drain.
+template <int SLOTS, int NPROD>
+__device__ __forceinline__ void t128_produce(const CUtensorMap* tmk, const CUtensorMap* tmv,
+                                             const TcParams& p, int b, int h, int kb0,
+                                             int nblk_seq, int n_tiles, int rot, int pw, int lane,
+                                             unsigned char* ring, uint64_t* full, uint64_t* empty,
+                                             volatile int* s_abort, volatile int* s_issued) {
+    constexpr int BPT = kT128Keys / kBlockTok;              // 8 pool blocks per key tile
+    constexpr int SLOT = kT128Keys * 128 * 2;               // two 64-dim halves
+    const int32_t* tab = p.tables + (int64_t)b * p.table_stride;
+    const int first_id = kb0 < nblk_seq ? tab[kb0] : 0;
+    int my_blocks = 0;
+    for (int k = pw; k < BPT; k += NPROD) ++my_blocks;
+    // block ids of four key tiles, one per lane, for the K and the V stream
+    int ids_k = 0, ids_v = 0;
+    for (int q = 0; q < 2 * n_tiles; ++q) {
+        bool is_v;
+        int i;
+        t128_item(q, n_tiles, is_v, i);
+        i += rot;                                           // key tile actually read
+        if (i >= n_tiles) i -= n_tiles;
+        if ((i * BPT) % 32 == 0 || q < 2 || (is_v && q < 4)) {
+            // first tile of a stream, or a new group of four tiles
+            const int blk = kb0 + (i & ~3) * BPT + lane;
+            int id = blk < nblk_seq ? tab[blk] : first_id;
+            if (id < 0 || id >= p.n_blocks) {
+                raise_flag(CX_DEV_BAD_BLOCK);
+                id = 0;
+            }
+            if (is_v) ids_v = id; else ids_k = id;
+        }
+        const int ids = is_v ? ids_v : ids_k;
+        const int s = q % SLOTS;
+        const int use = q / SLOTS;
+        bool go = true;
+        if (lane == 0 && use > 0 &&
+            !mbar_wait_bounded(&empty[s], (use - 1) & 1, s_abort, kWaitLimitNs))
+            go = false;
+        go = __shfl_sync(0xffffffffu, go, 0) && !*s_abort;
+        if (!bar_red_and(1, 32 * NPROD, go)) {
+            if (lane == 0) {
+                *s_abort = 1;
+                raise_flag(CX_DEV_WAIT_TIMEOUT);
+            }
+            break;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], my_blocks * (SLOT / BPT));
+        unsigned char* dst = ring + s * SLOT;
+        for (int k = pw; k < BPT; k += NPROD) {
+            const int id = __shfl_sync(0xffffffffu, ids, (i * BPT + k) & 31);
+            if (lane == 0) {
+                const int z = (p.layer * p.n_blocks + id) * p.hk + h;
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf)
+                    tma_load_3d(dst + hf * (SLOT / 2) + k * 2048, is_v ? tmv : tmk, &full[s],
+                                hf * 64, 0, z);
+            }
+        }
+        if (pw == 0 && lane == 0) *s_issued = q + 1;
+    }
+}
+
 // tcgen05.mma with the A operand (M x 16, bf16 pairs per 32-bit column, row i
 // in lane i) read from TMEM.
 __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
@@ -244,63 +312,9 @@ __global__ void __launch_bounds__(T128Cfg::THREADS, 1)
     }
 
     if (warp >= C::PRODUCER_WARP && warp < C::PRODUCER_WARP + C::N_PRODUCERS) {
-        // ---------------- TMA producers: ring items in the order t128_item gives ----------------
-        // Producer pw loads blocks pw, pw + 3, ... of each item.  The three warps
-        // decide together at a named barrier whether an item goes ahead, so an
-        // item is issued by all of them or by none and `s_issued` stays exact.
-        const int pw = warp - C::PRODUCER_WARP;
-        const int32_t* tab = p.tables + (int64_t)b * p.table_stride;
-        const int first_id = kb0 < nblk_seq ? tab[kb0] : 0;
-        constexpr int BPT = kT128Keys / kBlockTok;          // 8 pool blocks per key tile
-        int my_blocks = 0;
-        for (int k = pw; k < BPT; k += C::N_PRODUCERS) ++my_blocks;
-        // block ids of four key tiles, one per lane, for the K and the V stream
-        int ids_k = 0, ids_v = 0;
-        for (int q = 0; q < 2 * n_tiles; ++q) {
-            bool is_v;
-            int i;
-            t128_item(q, n_tiles, is_v, i);
-            i += rot;                                       // key tile actually read
-            if (i >= n_tiles) i -= n_tiles;
-            if ((i * BPT) % 32 == 0 || q < 2 || (is_v && q < 4)) {
-                // first tile of a stream, or a new group of four tiles
-                const int blk = kb0 + (i & ~3) * BPT + lane;
-                int id = blk < nblk_seq ? tab[blk] : first_id;
-                if (id < 0 || id >= p.n_blocks) {
-                    raise_flag(CX_DEV_BAD_BLOCK);
-                    id = 0;
-                }
-                if (is_v) ids_v = id; else ids_k = id;
-            }
-            const int ids = is_v ? ids_v : ids_k;
-            const int s = q % kT128Slots;
-            const int use = q / kT128Slots;
-            bool go = true;
-            if (lane == 0 && use > 0 &&
-                !mbar_wait_bounded(&empty[s], (use - 1) & 1, s_abort, kWaitLimitNs))
-                go = false;
-            go = __shfl_sync(0xffffffffu, go, 0) && !*s_abort;
-            if (!bar_red_and(1, 32 * C::N_PRODUCERS, go)) {
-                if (lane == 0) {
-                    *s_abort = 1;
-                    raise_flag(CX_DEV_WAIT_TIMEOUT);
-                }
-                break;
-            }
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], my_blocks * 2 * C::KV_HALF / BPT);
-            unsigned char* dst = ring + s * C::SLOT;
-            for (int k = pw; k < BPT; k += C::N_PRODUCERS) {
-                const int id = __shfl_sync(0xffffffffu, ids, (i * BPT + k) & 31);
-                if (lane == 0) {
-                    const int z = (p.layer * p.n_blocks + id) * p.hk + h;
-#pragma unroll
-                    for (int hf = 0; hf < 2; ++hf)
-                        tma_load_3d(dst + hf * C::KV_HALF + k * 2048, is_v ? &tmv : &tmk,
-                                    &full[s], hf * 64, 0, z);
-                }
-            }
-            if (pw == 0 && lane == 0) *s_issued = q + 1;
-        }
+        t128_produce<kT128Slots, C::N_PRODUCERS>(&tmk, &tmv, p, b, h, kb0, nblk_seq, n_tiles, rot,
+                                                 warp - C::PRODUCER_WARP, lane, ring, full,
+                                                 empty, s_abort, s_issued);
     } else if (warp == C::MMA_WARP) {
         // ---------------- MMA issuer ----------------
         named_bar_sync(3, 256 + 32);                   // Q is in TMEM
