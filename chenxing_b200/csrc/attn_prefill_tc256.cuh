@@ -12,23 +12,29 @@
 // 128 packed rows each (row r of tile w: token t0 + w * tpt + r / G, query head
 // h * G + r % G).  Twelve warps:
 //
-//   producer warps : t128_produce, three warps, a ring of three 32 KB slots
-//                    holding K(0), K(1), V(0), K(2), V(1), ... ;
+//   producer warps : t128_produce, three warps, a ring of five 32 KB slots
+//                    loaded in the order K(0), K(1), V(0), K(2), V(1), ... ;
 //   MMA warp       : one thread issues S_w(i) = Q_w K(i)^T into TMEM
 //                    [128 w, 128 w + 128) and O_w += P_w(i) V(i) into TMEM
-//                    [256 + 128 w, ...), in the order S_0(i+1), PV_0(i),
-//                    S_1(i+1), PV_1(i): the next scores of a tile are computed
-//                    while its softmax finishes and the other tile's runs;
+//                    [256 + 128 w, ...) with P_w read from TMEM, in the order
+//                    PV_0(i), S_0(i+1), PV_1(i), S_1(i+1): while one tile's
+//                    softmax runs, the tensor pipe works on the other tile;
 //   warpgroup w    : softmax of query tile w, thread r owning row r (TMEM lane
 //                    r), in two passes over its 128 S columns (row max, then
-//                    exponentials) so no thread holds the whole row; S_w is
-//                    released after the second pass's TMEM reads, bf16 P_w goes
-//                    to shared memory (swizzled K-major) once PV_w(i-1) has
-//                    completed; lazy O rescale (only when a row max grows by
-//                    more than 2^8; a stale max is exact after the final
-//                    division); fp32 output rows in the epilogue.
+//                    exponentials) so no thread holds the whole row; bf16 P_w
+//                    is written back over the first 64 columns of S_w (keys
+//                    2c, 2c + 1 in column c: keys 0-63 only after S columns
+//                    0-63 were read, keys 64-127 after the rest); lazy O
+//                    rescale (only when a row max grows by more than 2^8; a
+//                    stale max is exact after the final division); fp32 output
+//                    rows in the epilogue.
 //
-// Q_0, Q_1 and P_0, P_1 live in shared memory (32 KB each).  Every wait is
+// The MMAs of one thread complete in issue order, so S_w(i) being ready means
+// PV_w(i-1) has read P_w(i-1) and finished accumulating O_w: the softmax needs
+// no other wait before rescaling O_w or writing P_w(i), and S_w(i+1), issued
+// after PV_w(i), never overwrites a P that is still to be read.
+//
+// Q_0, Q_1 live in shared memory (32 KB each).  Every wait is
 // bounded; on a timeout the CTA raises CX_DEV_WAIT_TIMEOUT, drains its own
 // copies and MMAs, frees its TMEM and returns.  tcgen05.ld / tcgen05.st are
 // warp-collective, so every branch around them is decided warp-uniformly.
@@ -37,7 +43,13 @@
 
 namespace cx {
 
-constexpr int kT256Slots = 3;    // ring slots, one K or V tile each
+constexpr int kT256Slots = 5;    // ring slots, one K or V tile each
+
+// Ring position of K(j) and V(j) among n key tiles (the order t128_item gives).
+__device__ __forceinline__ int t128_pos_k(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__device__ __forceinline__ int t128_pos_v(int j, int n) {
+    return n == 1 ? 1 : (j == n - 1 ? 2 * n - 1 : 2 * j + 2);
+}
 
 struct T256Cfg {
     static constexpr int D = 128;
@@ -45,14 +57,11 @@ struct T256Cfg {
     static constexpr int Q_BYTES = 2 * Q_HALF;              // one query tile
     static constexpr int KV_HALF = kT128Keys * 128;         // 16 KB: 128 keys x 128 B
     static constexpr int SLOT = 2 * KV_HALF;                // one K or V tile
-    static constexpr int P_HALF = kTcRows * 128;            // 64-key half of P
-    static constexpr int P_BYTES = 2 * P_HALF;              // one P tile
     static constexpr int OFF_Q = 0;                         // Q_0, Q_1
-    static constexpr int OFF_P = OFF_Q + 2 * Q_BYTES;       // P_0, P_1
-    static constexpr int OFF_RING = OFF_P + 2 * P_BYTES;
+    static constexpr int OFF_RING = OFF_Q + 2 * Q_BYTES;
     static constexpr int OFF_BAR = OFF_RING + kT256Slots * SLOT;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;       // + 1 KB alignment slack
-    static constexpr int TMEM_COLS = 512;                   // S_0, S_1, O_0, O_1
+    static constexpr int TMEM_COLS = 512;                   // S_0 / P_0, S_1 / P_1, O_0, O_1
     static constexpr int N_PRODUCERS = 3;
     static constexpr int THREADS = 384;                     // softmax 2 x 4, producers 3, MMA
     static constexpr int PRODUCER_WARP = 8;                 // first producer warp
@@ -70,13 +79,11 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* sq = sm + C::OFF_Q;
-    unsigned char* sp = sm + C::OFF_P;
     unsigned char* ring = sm + C::OFF_RING;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
     uint64_t* full = bars;                     // [kT256Slots] slot loaded
     uint64_t* empty = bars + kT256Slots;       // [kT256Slots] slot read by its MMAs
     uint64_t* s_full = bars + 2 * kT256Slots;  // [2] S_w ready in TMEM
-    uint64_t* s_free = s_full + 2;             // [2] S_w read by its softmax
     uint64_t* p_full = s_full + 4;             // [2] P_w written, O_w rescaled
     uint64_t* o_done = s_full + 6;             // [2] PV_w completed
     uint64_t* mma_drain = s_full + 8;          // last commit of the MMA thread
@@ -119,7 +126,6 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
         }
         for (int w = 0; w < 2; ++w) {
             mbar_init(&s_full[w], 1);
-            mbar_init(&s_free[w], 128);
             mbar_init(&p_full[w], 128);
             mbar_init(&o_done[w], 1);
         }
@@ -200,15 +206,15 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
         if (lane == 0) {
             constexpr uint32_t idesc_s = tc_idesc(kTcRows, kT128Keys, 0);
             constexpr uint32_t idesc_o = tc_idesc(kTcRows, D, 1);
-            const uint32_t q_base = smem_addr(sq), p_base = smem_addr(sp);
+            const uint32_t q_base = smem_addr(sq);
             const uint32_t r_base = smem_addr(ring);
             bool ok = true;
-            int q = 0;                                 // next ring item (t128_item order)
-            auto wait_item = [&]() {
-                const bool r = mbar_wait_bounded(&full[q % kT256Slots], (q / kT256Slots) & 1,
-                                                 s_abort, kWaitLimitNs);
+            // wait for the ring item at position `pos`; returns its slot or -1
+            auto wait_pos = [&](int pos) {
+                const bool r = mbar_wait_bounded(&full[pos % kT256Slots],
+                                                 (pos / kT256Slots) & 1, s_abort, kWaitLimitNs);
                 if (r) tc_fence_after();
-                return r;
+                return r ? pos % kT256Slots : -1;
             };
             auto wait_bar = [&](uint64_t* bar, int parity) {
                 const bool r = mbar_wait_bounded(bar, parity & 1, s_abort, kWaitLimitNs);
@@ -228,24 +234,21 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
                 tc_commit(&s_full[w]);
             };
             // O_w += P_w V from the V tile in `slot`: K = 128 keys in steps of 16;
-            // P K-major (64-key halves P_HALF apart), V MN-major (64-dim halves
-            // KV_HALF apart, 8-key groups 1 KB apart)
+            // P_w from TMEM (8 columns of bf16 pairs per step), V MN-major
+            // (64-dim halves KV_HALF apart, 8-key groups 1 KB apart)
             auto issue_pv = [&](int w, int slot, bool acc) {
                 const uint32_t v_base = r_base + slot * C::SLOT;
-                const uint32_t pw = p_base + w * C::P_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < kT128Keys / 16; ++kk)
-                    tc_mma(tmem + 2 * kT128Keys + w * D,
-                           tc_sdesc(pw + (kk >> 2) * C::P_HALF + (kk & 3) * 32, 16, 1024),
-                           tc_sdesc(v_base + kk * 2048, C::KV_HALF, 1024), idesc_o,
-                           (acc || kk > 0) ? 1u : 0u);
+                    tc_mma_ts(tmem + 2 * kT128Keys + w * D, tmem + w * kT128Keys + kk * 8,
+                              tc_sdesc(v_base + kk * 2048, C::KV_HALF, 1024), idesc_o,
+                              (acc || kk > 0) ? 1u : 0u);
                 tc_commit(&o_done[w]);
             };
             if (n_tiles > 0) {
-                ok = wait_item();                      // K(0)
+                const int ks = wait_pos(t128_pos_k(0));
+                ok = ks >= 0;
                 if (ok) {
-                    const int ks = q % kT256Slots;
-                    ++q;
                     issue_s(0, ks);
                     if (nq == 2) issue_s(1, ks);
                     tc_commit(&empty[ks]);
@@ -253,26 +256,23 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
             }
             for (int i = 0; ok && i < n_tiles; ++i) {
                 const bool next = i + 1 < n_tiles;
+                const int vs = wait_pos(t128_pos_v(i, n_tiles));
+                ok = vs >= 0;
+                if (!ok) break;
                 int ks = 0;
-                if (next) {                            // K(i+1) comes before V(i) in the ring
-                    if (!(ok = wait_item())) break;
-                    ks = q % kT256Slots;
-                    ++q;
+                if (next) {
+                    ks = wait_pos(t128_pos_k(i + 1));
+                    ok = ks >= 0;
+                    if (!ok) break;
                 }
-                if (!(ok = wait_item())) break;        // V(i)
-                const int vs = q % kT256Slots;
-                ++q;
                 for (int w = 0; ok && w < nq; ++w) {
-                    if (next) {
-                        if (!(ok = wait_bar(&s_free[w], i))) break;
-                        issue_s(w, ks);
-                    }
                     if (!(ok = wait_bar(&p_full[w], i))) break;
                     issue_pv(w, vs, i > 0);
+                    if (next) issue_s(w, ks);          // after PV_w(i) has been issued
                 }
                 if (!ok) break;
-                if (next) tc_commit(&empty[ks]);
                 tc_commit(&empty[vs]);
+                if (next) tc_commit(&empty[ks]);
             }
             if (!ok) {
                 *s_abort = 1;
@@ -286,7 +286,6 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t tm_s = tmem + w * kT128Keys + lane_off;
         const uint32_t tm_o = tmem + 2 * kT128Keys + w * D + lane_off;
-        unsigned char* pw = sp + w * C::P_BYTES;
         const int tw0 = t0 + w * tpt;                            // first token of this tile
         const int tw1 = min(t_end, tw0 + tpt);
         const int t = tw0 + r / G;
@@ -339,14 +338,8 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
             const float m_use = m_new == -INFINITY ? 0.f : m_new;
             const float alpha = grow ? exp2f(m - m_use) : 1.f;
             m = m_new;
+            // O_w holds PV_w(0 .. i-1): S_w(i) was issued after PV_w(i-1)
             if (i > 0) {
-                // P_w and O_w are busy until PV_w(i-1) has completed
-                if (!__all_sync(0xffffffffu, mbar_wait_bounded(&o_done[w], (i - 1) & 1,
-                                                                s_abort, kWaitLimitNs))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
                 if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
                     for (int c = 0; c < D / 32; ++c) {
@@ -360,8 +353,8 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
                     tc_wait_st();
                 }
             }
-            // pass 2: p = 2^(s * scale - m), 64 columns at a time, bf16 P row
-            // into shared memory; S_w is released after the last TMEM read
+            // pass 2: p = 2^(s * scale - m), 64 columns at a time, bf16 pairs
+            // written back over S_w columns [32 hh, 32 hh + 32)
             float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
@@ -369,10 +362,6 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
                 tc_ld32(tm_s + hh * 64, &v[0]);
                 tc_ld32(tm_s + hh * 64 + 32, &v[32]);
                 tc_wait_ld();
-                if (hh == 1) {
-                    tc_fence_before();
-                    mbar_arrive(&s_free[w]);           // S_w may be overwritten now
-                }
                 if (edge) {
 #pragma unroll
                     for (int j = 0; j < 64; ++j) {
@@ -388,18 +377,15 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
                         ps[j & 7] += v[j];
                     }
                 }
+                float pk[32];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint4 v4 = make_uint4(pack_bf16(v[c * 8 + 0], v[c * 8 + 1]),
-                                                pack_bf16(v[c * 8 + 2], v[c * 8 + 3]),
-                                                pack_bf16(v[c * 8 + 4], v[c * 8 + 5]),
-                                                pack_bf16(v[c * 8 + 6], v[c * 8 + 7]));
-                    *reinterpret_cast<uint4*>(pw + tc_swz(r, hh * 64 + c * 8, kTcRows)) = v4;
-                }
+                for (int c = 0; c < 32; ++c)
+                    pk[c] = __uint_as_float(pack_bf16(v[2 * c], v[2 * c + 1]));
+                tc_st32(tm_s + hh * 32, pk);
             }
             l = l * alpha +
                 (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
-            fence_async_smem();
+            tc_wait_st();
             tc_fence_before();
             mbar_arrive(&p_full[w]);
         }
