@@ -153,33 +153,36 @@ __global__ void __launch_bounds__(256) kv_append_vec_kernel(
         for (int64_t t0 = blockIdx.x; t0 < n_tok; t0 += (int64_t)gridDim.x * kUnroll) {
             float x[kRaw ? 1 : kUnroll][8];
             uint4 raw[kRaw ? kUnroll : 1];
-            int64_t dst[kUnroll];
+            int64_t slot[kUnroll];
+            // the row loads do not wait for the slot loads (a skipped token's
+            // source row is still valid memory), so all of them are in flight
+            // together
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
                 const int64_t t = t0 + (int64_t)u * gridDim.x;
-                dst[u] = -1;
+                slot[u] = -1;
                 if (t < n_tok) {
-                    const int64_t slot = slots[t];
-                    if (slot >= cap) {
-                        if (c0 == 0) raise_flag(CX_DEV_BAD_SLOT);
-                    } else if (slot >= 0) {
-                        const uint32_t blk = (uint32_t)slot / bs;
-                        const uint32_t off = (uint32_t)slot - blk * bs;
-                        dst[u] = (int64_t)blk * blk_stride + (int64_t)off * D;
-                        if constexpr (kRaw)
-                            raw[u] = *reinterpret_cast<const uint4*>(src + t * H * D);
-                        else
-                            Vec8<S>::load(src + t * H * D, x[u]);
-                    }
+                    slot[u] = slots[t];
+                    if constexpr (kRaw)
+                        raw[u] = *reinterpret_cast<const uint4*>(src + t * H * D);
+                    else
+                        Vec8<S>::load(src + t * H * D, x[u]);
                 }
             }
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
-                if (dst[u] < 0) continue;
+                if (slot[u] >= cap) {
+                    if (c0 == 0) raise_flag(CX_DEV_BAD_SLOT);
+                    continue;
+                }
+                if (slot[u] < 0) continue;
+                const uint32_t blk = (uint32_t)slot[u] / bs;
+                const uint32_t off = (uint32_t)slot[u] - blk * bs;
+                const int64_t dst = (int64_t)blk * blk_stride + (int64_t)off * D;
                 if constexpr (kRaw)
-                    *reinterpret_cast<uint4*>(dstp + dst[u]) = raw[u];
+                    *reinterpret_cast<uint4*>(dstp + dst) = raw[u];
                 else
-                    Vec8<P>::store(dstp + dst[u], x[u]);
+                    Vec8<P>::store(dstp + dst, x[u]);
             }
         }
     }
