@@ -46,13 +46,15 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["cfg2", "small", "prefill", "prefill-small", "append",
-                                         "cfg4"],
+                                         "cfg4", "copy"],
                     default="cfg2",
                     help="small: 1 layer, pool sized to need (~2 GB, for profiler captures); "
                          "prefill: chunked-prefill attention on the tcgen05 kernel (its own "
                          "JSON line, TFLOP/s); prefill-small: the same, 2 sequences; "
                          "append: prefill-sized KV append (its own JSON line, GB/s); "
-                         "cfg4: speculative verify, gamma 4 and 8 (their own JSON lines)")
+                         "cfg4: speculative verify, gamma 4 and 8 (their own JSON lines); "
+                         "copy: block copy (compaction) and read_layer gather (their own "
+                         "JSON lines, GB/s)")
     ap.add_argument("--pool-frac", type=float, default=0.9)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -750,6 +752,87 @@ def run_append(args):
 
 
 # ---------------------------------------------------------------------------
+# block copy (compaction) and read_layer gather (separate mode, not the headline)
+# ---------------------------------------------------------------------------
+def run_copy(args):
+    """Two HBM-bound data movers, each with its own JSON line.
+    cx_block_copy: a compaction moving 8192 whole blocks over 4 layers (src and
+    dst disjoint, ids from a seeded permutation); algorithmic bytes = K and V
+    tiles read + written + the two int32 id arrays.
+    cx_kv_gather (read_layer): 262144 tokens of one layer gathered from
+    scattered blocks into contiguous [tokens][Hkv][D] K and V; algorithmic
+    bytes = rows read + written + the int32 block table."""
+    import torch
+    from chenxing_b200 import RadixPagedKVCache, _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rng = np.random.default_rng(args.seed)
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    peak, kind = measured_peak()
+
+    def timed(launch):
+        for _ in range(args.warmup):
+            launch()
+        torch.cuda.synchronize(dev)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for e0, e1 in evs:
+            e0.record(stream)
+            launch()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        if _lib.device_flags(clear=True):
+            raise RuntimeError("device flags raised during the copy bench")
+        return float(np.mean([a.elapsed_time(b) for a, b in evs]))
+
+    def line(metric, kernel, alg, avg, workload):
+        gbs = alg / (avg / 1e3) / 1e9
+        print(json.dumps({
+            "metric": metric, "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": avg, "higher_is_better": True,
+            "scaling": "none", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": workload, "kv_heads": HK, "head_dim": D, "block_size": BS,
+                       "l2": "> 126 MB moved per launch"},
+            "roofline": {"bound": "hbm", "kernel": kernel, "achieved": gbs, "peak": peak,
+                         "unit": "GB/s", "frac": gbs / peak, "peak_source": kind,
+                         "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg}}), flush=True)
+
+    # compaction: 8192 block moves over 4 layers
+    L, NB, n = 4, 32768, 8192
+    cache = RadixPagedKVCache(NB, BS, L, HK, D, dtype="bfloat16", device=dev, host_io=False)
+    perm = rng.permutation(NB).astype(np.int32)
+    src = torch.from_numpy(perm[:n].copy()).to(dev)
+    dst = torch.from_numpy(perm[n:2 * n].copy()).to(dev)
+    pool = cache.cx_pool()
+    avg = timed(lambda: _lib.check(lib.cx_block_copy(pool, src.data_ptr(), dst.data_ptr(), n,
+                                                     BS, sp), "cx_block_copy"))
+    alg = 2 * 2 * n * L * HK * BS * D * ELEM + 8 * n
+    line("block copy GB/s (cx_block_copy, compaction of 8192 blocks x 4 layers)",
+         "block_copy_kernel", alg, avg, f"{n} block moves x {L} layers, K and V")
+    del cache
+    torch.cuda.empty_cache()
+
+    # read_layer: 262144 tokens gathered from scattered blocks
+    n_tok = 262144
+    nb = n_tok // BS
+    cache = RadixPagedKVCache(nb + 16, BS, 1, HK, D, dtype="bfloat16", device=dev,
+                              host_io=False)
+    table = torch.from_numpy(rng.permutation(nb + 16)[:nb].astype(np.int32)).to(dev)
+    ko = torch.empty((n_tok, HK, D), dtype=torch.bfloat16, device=dev)
+    vo = torch.empty_like(ko)
+    pool = cache.cx_pool()
+    avg = timed(lambda: _lib.check(lib.cx_kv_gather(pool, 0, table.data_ptr(), n_tok,
+                                                    ko.data_ptr(), vo.data_ptr(), sp),
+                                   "cx_kv_gather"))
+    alg = 2 * 2 * n_tok * HK * D * ELEM + 4 * nb
+    line("read_layer gather GB/s (cx_kv_gather, 262144 tokens)", "kv_gather_kernel", alg, avg,
+         f"{n_tok} tokens of one layer from scattered blocks")
+
+
+# ---------------------------------------------------------------------------
 # cfg4: speculative verify (separate mode, not the headline)
 # ---------------------------------------------------------------------------
 def run_verify(args):
@@ -857,6 +940,8 @@ def main():
         run_append(args)
     elif args.config == "cfg4":
         run_verify(args)
+    elif args.config == "copy":
+        run_copy(args)
     else:
         run_ours(args)
 

@@ -311,6 +311,107 @@ __global__ void __launch_bounds__(256) block_copy_kernel(
     }
 }
 
+// 16-byte variants of the two movers above (rows a multiple of 16 bytes,
+// 16-byte aligned buffers).  A pool block's K (or V) rows of all heads are one
+// contiguous region [H][block_size][D], so a job is a whole region where it
+// can be: each thread keeps kMoveUnroll 16-byte loads of it in flight before
+// its stores, and one block-id load serves the whole region.
+constexpr int kMoveUnroll = 8;
+
+// Block copy: job = (pair i, layer, head group, K|V) of `hj` heads' first
+// n_slots rows; `hj` = H when whole blocks move (one contiguous region),
+// else 1 (a partial tail per head).  `cj` = 16-byte chunks per job.
+__global__ void __launch_bounds__(256) block_copy_vec_kernel(
+    uint4* __restrict__ kp, uint4* __restrict__ vp, PoolGeom g, int eb,
+    const int32_t* __restrict__ src, const int32_t* __restrict__ dst, int64_t n, int hj,
+    int cj) {
+    const uint32_t groups = (uint32_t)(g.n_kv_heads / hj);
+    const int64_t n_jobs = n * g.n_layers * groups * 2;
+    for (int64_t job = blockIdx.x; job < n_jobs; job += gridDim.x) {
+        // 32-bit index math (the host guarantees n_jobs < 2^31)
+        uint32_t r = (uint32_t)job >> 1;
+        const uint32_t hg = r % groups;
+        r /= groups;
+        const uint32_t layer = r % (uint32_t)g.n_layers;
+        const uint32_t i = r / (uint32_t)g.n_layers;
+        const int64_t sb = src[i], db = dst[i];
+        if (sb < 0 || sb >= g.n_blocks || db < 0 || db >= g.n_blocks) {
+            if (threadIdx.x == 0) raise_flag(CX_DEV_BAD_BLOCK);
+            continue;
+        }
+        uint4* base = (job & 1) ? vp : kp;
+        const uint4* s = base + g.tile(layer, sb, (int64_t)hg * hj) * eb / 16;
+        uint4* d = base + g.tile(layer, db, (int64_t)hg * hj) * eb / 16;
+        // a head group's rows: hj tiles of cj / hj chunks, tile stride = a full tile
+        const int per_tile = cj / hj;
+        const int tile_chunks = (int)(g.block_size * g.head_dim * eb / 16);
+        for (int k0 = threadIdx.x; k0 < cj; k0 += blockDim.x * kMoveUnroll) {
+            uint4 buf[kMoveUnroll];
+            int off[kMoveUnroll];
+#pragma unroll
+            for (int u = 0; u < kMoveUnroll; ++u) {
+                const int k = k0 + u * blockDim.x;
+                off[u] = -1;
+                if (k < cj) {
+                    const int tt = k / per_tile;
+                    off[u] = tt * tile_chunks + (k - tt * per_tile);
+                    buf[u] = s[off[u]];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kMoveUnroll; ++u)
+                if (off[u] >= 0) d[off[u]] = buf[u];
+        }
+    }
+}
+
+// read_layer gather: job = (table block jb, K|V): the block's contiguous
+// [H][block_size][D] region is read in order and written to token rows
+// [jb * block_size + slot][head][D] (rows past n_tok are skipped).
+__global__ void __launch_bounds__(256) kv_gather_vec_kernel(
+    const uint4* __restrict__ kp, const uint4* __restrict__ vp, PoolGeom g, int64_t layer,
+    int eb, const int32_t* __restrict__ table, int64_t n_tok, uint4* __restrict__ ko,
+    uint4* __restrict__ vo) {
+    const int H = (int)g.n_kv_heads;
+    const int bs = (int)g.block_size;
+    const int cpr = (int)(g.head_dim * eb / 16);          // chunks per row
+    const int cj = H * bs * cpr;                          // chunks per region
+    const int64_t n_blk = (n_tok + bs - 1) / bs;
+    for (int64_t job = blockIdx.x; job < 2 * n_blk; job += gridDim.x) {
+        const int64_t jb = job >> 1;
+        const int64_t blk = table[jb];
+        if (blk < 0 || blk >= g.n_blocks) {
+            if (threadIdx.x == 0) raise_flag(CX_DEV_BAD_BLOCK);
+            continue;
+        }
+        const bool is_v = job & 1;
+        const uint4* s = (is_v ? vp : kp) + g.tile(layer, blk, 0) * eb / 16;
+        uint4* o = is_v ? vo : ko;
+        const int rows = (int)min((int64_t)bs, n_tok - jb * bs);   // valid slots
+        for (int k0 = threadIdx.x; k0 < cj; k0 += blockDim.x * kMoveUnroll) {
+            uint4 buf[kMoveUnroll];
+            int64_t dst[kMoveUnroll];
+#pragma unroll
+            for (int u = 0; u < kMoveUnroll; ++u) {
+                const int k = k0 + u * blockDim.x;
+                dst[u] = -1;
+                if (k < cj) {
+                    const int h = k / (bs * cpr);
+                    const int rem = k - h * bs * cpr;
+                    const int slot = rem / cpr, c = rem - slot * cpr;
+                    if (slot < rows) {
+                        dst[u] = ((jb * bs + slot) * H + h) * cpr + c;
+                        buf[u] = s[k];
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kMoveUnroll; ++u)
+                if (dst[u] >= 0) o[dst[u]] = buf[u];
+        }
+    }
+}
+
 static int check_pool(const cx_pool* p) {
     if (!p) return fail(CX_ERR_SHAPE, "pool is NULL");
     if (!p->k || !p->v) return fail(CX_ERR_SHAPE, "pool buffers are NULL");
@@ -458,6 +559,17 @@ int cx_kv_gather(const cx_pool* pool, int64_t layer, const int32_t* block_table,
     if (n_tokens == 0) return CX_OK;
     if (!block_table || !k_out || !v_out) return fail(CX_ERR_SHAPE, "cx_kv_gather: NULL array");
     const int eb = elem_bytes(pool->dtype);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(pool->k) | reinterpret_cast<uintptr_t>(pool->v) |
+                         reinterpret_cast<uintptr_t>(k_out) | reinterpret_cast<uintptr_t>(v_out);
+    if ((pool->head_dim * eb) % 16 == 0 && (al & 15) == 0 && n_tokens < (1ll << 31) &&
+        pool->n_kv_heads * pool->block_size * (pool->head_dim * eb / 16) < (1ll << 30)) {
+        const int64_t jobs = 2 * ((n_tokens + pool->block_size - 1) / pool->block_size);
+        kv_gather_vec_kernel<<<grid_for(jobs, 1), 256, 0, as_stream(stream)>>>(
+            static_cast<const uint4*>(pool->k), static_cast<const uint4*>(pool->v),
+            geom_of(pool), layer, eb, block_table, n_tokens, static_cast<uint4*>(k_out),
+            static_cast<uint4*>(v_out));
+        return check_launch("kv_gather_vec_kernel");
+    }
     kv_gather_kernel<<<grid_for(n_tokens * pool->n_kv_heads, 8), 256, 0, as_stream(stream)>>>(
         static_cast<const char*>(pool->k), static_cast<const char*>(pool->v), geom_of(pool), layer,
         eb, block_table, n_tokens, static_cast<char*>(k_out), static_cast<char*>(v_out));
@@ -474,6 +586,21 @@ int cx_block_copy(const cx_pool* pool, const int32_t* src, const int32_t* dst, i
     if (n == 0 || n_slots == 0) return CX_OK;
     if (!src || !dst) return fail(CX_ERR_SHAPE, "cx_block_copy: NULL id arrays");
     const int64_t jobs = n * pool->n_layers * pool->n_kv_heads * 2;
+    const int eb = elem_bytes(pool->dtype);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(pool->k) | reinterpret_cast<uintptr_t>(pool->v);
+    const int64_t region = pool->n_kv_heads * pool->block_size * pool->head_dim * eb / 16;
+    if ((pool->head_dim * eb) % 16 == 0 && (al & 15) == 0 && jobs < (1ll << 31) &&
+        region < (1ll << 30)) {
+        // whole blocks: one contiguous region per (pair, layer, K|V); a partial
+        // tail: per head
+        const int hj = n_slots == pool->block_size ? (int)pool->n_kv_heads : 1;
+        const int cj = (int)(hj * n_slots * pool->head_dim * eb / 16);
+        const int64_t vjobs = n * pool->n_layers * (pool->n_kv_heads / hj) * 2;
+        block_copy_vec_kernel<<<grid_for(vjobs, 1), 256, 0, as_stream(stream)>>>(
+            static_cast<uint4*>(pool->k), static_cast<uint4*>(pool->v), geom_of(pool), eb, src,
+            dst, n, hj, cj);
+        return check_launch("block_copy_vec_kernel");
+    }
     block_copy_kernel<<<grid_for(jobs, 1), 256, 0, as_stream(stream)>>>(
         static_cast<char*>(pool->k), static_cast<char*>(pool->v), geom_of(pool),
         elem_bytes(pool->dtype), src, dst, n, n_slots);

@@ -74,6 +74,30 @@ def test_read_layer_edge_cases_match_oracle():
         assert e[0].shape == (0, 3, 5)
 
 
+def test_read_layer_vector_path_partial_blocks_bit_exact():
+    """16-byte rows (bf16 D 128, fp32 D 64) take the whole-block gather
+    kernel; token counts that end inside a block, span one block exactly or
+    run past it must match the oracle bit for bit on every layer."""
+    from chenxing_b200 import RadixPagedKVCache
+    from oracle.radix_kv import OraclePagedKVCache
+    rng = np.random.default_rng(6)
+    for dtype, odt, d in (("bfloat16", gcases.BF16, 128), (np.float32, np.float32, 64)):
+        c = RadixPagedKVCache(12, 16, 2, 4, d, dtype=dtype)
+        o = OraclePagedKVCache(12, 16, 2, 4, d, dtype=odt)
+        table = [7, 2, 11, 0, 5]
+        k = rng.standard_normal((80, 4, d)).astype(np.float32)
+        v = rng.standard_normal((80, 4, d)).astype(np.float32)
+        for layer in (0, 1):
+            c.write_layer(table, 0, layer, k * (layer + 1), v - layer)
+            o.write_layer(table, 0, layer, k * (layer + 1), v - layer)
+        for n in (1, 15, 16, 17, 33, 64, 79, 80):
+            for layer in (0, 1):
+                a, b = c.read_layer(table, n, layer), o.read_layer(table, n, layer)
+                assert a[0].shape == b[0].shape == (n, 4, d)
+                assert np.array_equal(np.asarray(a[0]).view(np.uint8), np.asarray(b[0]).view(np.uint8))
+                assert np.array_equal(np.asarray(a[1]).view(np.uint8), np.asarray(b[1]).view(np.uint8))
+
+
 def test_pool_view_has_reference_axis_order():
     from chenxing_b200 import RadixPagedKVCache
     c = RadixPagedKVCache(3, 4, 2, 2, 8)
