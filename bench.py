@@ -750,6 +750,49 @@ def run_append(args):
                      "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_source": kind,
                      "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg}}), flush=True)
 
+    # the same append with RoPE fused (cx_kv_append_rope): K rotated into the
+    # pool, V copied, Q of Hq heads rotated into a bf16 q_out
+    from chenxing_b200.rope import build_rope_cache
+    cos, sin = build_rope_cache(T, D)
+    cos_t = torch.from_numpy(cos).to(dev)
+    sin_t = torch.from_numpy(sin).to(dev)
+    pos = torch.arange(T, dtype=torch.int64, device=dev).repeat(B)
+    q = torch.randn((n_tok, HQ, D), device=dev, generator=g).bfloat16()
+    q_out = torch.empty_like(q)
+
+    def launch_rope():
+        _lib.check(lib.cx_kv_append_rope(pool, 0, k.data_ptr(), v.data_ptr(), _lib.CX_BF16,
+                                         slots.data_ptr(), pos.data_ptr(), n_tok,
+                                         cos_t.data_ptr(), sin_t.data_ptr(), T, 0,
+                                         q.data_ptr(), HQ, q_out.data_ptr(), _lib.CX_BF16, sp),
+                   "cx_kv_append_rope")
+    for _ in range(args.warmup):
+        launch_rope()
+    torch.cuda.synchronize(dev)
+    for e0, e1 in evs:
+        e0.record(stream)
+        launch_rope()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    if _lib.device_flags(clear=True):
+        raise RuntimeError("device flags raised during the RoPE append bench")
+    avg = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    # K, V and Q rows read and written, slots and positions (the cos / sin
+    # rows are read once per token from cache, 1 KB per token)
+    alg = 2 * (2 * n_tok * HK * D * ELEM) + 2 * n_tok * HQ * D * ELEM + 16 * n_tok
+    gbs = alg / (avg / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "KV append with fused RoPE GB/s (cx_kv_append_rope, prefill-sized)",
+        "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": avg, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{B} sequences x {T} tokens, K / V appended and Q rotated "
+                               f"({HQ} heads), blocks scattered",
+                   "kv_heads": HK, "q_heads": HQ, "head_dim": D, "block_size": BS},
+        "roofline": {"bound": "hbm", "kernel": "kv_append_rope_kernel", "achieved": gbs,
+                     "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_source": kind,
+                     "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg}}), flush=True)
+
 
 # ---------------------------------------------------------------------------
 # block copy (compaction) and read_layer gather (separate mode, not the headline)

@@ -261,6 +261,128 @@ __global__ void __launch_bounds__(256) kv_append_rope_kernel(
     }
 }
 
+// Vector form of kv_append_rope_kernel: one thread per 8 rotation pairs of one
+// row (pairs p .. p+7: elements p.. and p+half.. half-split, 2p .. 2p+15
+// interleaved), 8-element vector accesses.  The position, slot and row loads
+// are all issued before any of them is checked, so their latencies overlap;
+// the cos / sin rows (shared by every row of the token, so cache hits) follow.
+// The same _rn products and sums as rope_pair, so the same bits.  The host
+// guarantees head_dim % 16 == 0, 16-byte aligned buffers and n_blocks *
+// block_size < 2^31.
+template <typename S, typename P, typename QO>
+__global__ void __launch_bounds__(256) kv_append_rope_vec_kernel(
+    P* __restrict__ kp, P* __restrict__ vp, PoolGeom g, int64_t layer,
+    const S* __restrict__ kn, const S* __restrict__ vn, const int64_t* __restrict__ slots,
+    const int64_t* __restrict__ positions, int64_t n_tok, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, int64_t rows, int inter, const S* __restrict__ q,
+    int hq, QO* __restrict__ q_out) {
+    const int H = (int)g.n_kv_heads, D = (int)g.head_dim, half = D / 2;
+    const int gpr = half / 8;                             // 8-pair groups per row
+    const int per_tok = (hq + 2 * H) * gpr;
+    const int64_t total = n_tok * per_tok;
+    const int64_t cap = g.n_blocks * g.block_size;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / per_tok;
+        const int rem = (int)(i - t * per_tok);
+        const int row = rem / gpr, p0 = (rem - row * gpr) * 8;
+        const bool is_q = row < hq;
+        const bool is_v = row >= hq + H;
+        const int h = row - hq - (is_v ? H : 0);
+        const int ea = inter ? 2 * p0 : p0, eb = inter ? 2 * p0 + 8 : p0 + half;
+        const S* x = is_q ? q + (t * hq + row) * D : (is_v ? vn : kn) + (t * H + h) * D;
+        // every load of this item first
+        const int64_t pos = positions[t];
+        const int64_t slot = is_q ? 0 : slots[t];
+        float fa[8], fb[8];
+        Vec8<S>::load(x + ea, fa);
+        Vec8<S>::load(x + eb, fb);
+        if (pos < 0 || pos >= rows) {
+            if (rem == 0) raise_flag(CX_DEV_BAD_POSITION);
+            continue;
+        }
+        int64_t dst = 0;
+        if (!is_q) {
+            if (slot < 0) continue;                       // padding token
+            if (slot >= cap) {
+                if (rem == 0) raise_flag(CX_DEV_BAD_SLOT);
+                continue;
+            }
+            const uint32_t blk = (uint32_t)slot / (uint32_t)g.block_size;
+            const uint32_t off = (uint32_t)slot - blk * (uint32_t)g.block_size;
+            dst = g.tile(layer, blk, h) + (int64_t)off * D;
+        }
+        float a[8], b[8];
+        if (inter) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                a[k] = fa[2 * k];
+                b[k] = fa[2 * k + 1];
+                a[k + 4] = fb[2 * k];
+                b[k + 4] = fb[2 * k + 1];
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                a[k] = fa[k];
+                b[k] = fb[k];
+            }
+        }
+        float oa[8], ob[8];
+        if (is_v) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                oa[k] = a[k];
+                ob[k] = b[k];
+            }
+        } else {
+            const float* cr = cos_t + pos * D;
+            const float* sr = sin_t + pos * D;
+            float c0[8], s0[8];
+            Vec8<float>::load(cr + p0, c0);
+            Vec8<float>::load(sr + p0, s0);
+            if (inter) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    oa[k] = __fsub_rn(__fmul_rn(a[k], c0[k]), __fmul_rn(b[k], s0[k]));
+                    ob[k] = __fadd_rn(__fmul_rn(a[k], s0[k]), __fmul_rn(b[k], c0[k]));
+                }
+            } else {
+                float c1[8], s1[8];
+                Vec8<float>::load(cr + p0 + half, c1);
+                Vec8<float>::load(sr + p0 + half, s1);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    oa[k] = __fadd_rn(__fmul_rn(a[k], c0[k]), __fmul_rn(-b[k], s0[k]));
+                    ob[k] = __fadd_rn(__fmul_rn(b[k], c1[k]), __fmul_rn(a[k], s1[k]));
+                }
+            }
+        }
+        auto put = [&](auto* y) {
+            using T = typename std::remove_pointer<decltype(y)>::type;
+            if (inter) {
+                float e0[8], e1[8];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    e0[2 * k] = oa[k];
+                    e0[2 * k + 1] = ob[k];
+                    e1[2 * k] = oa[k + 4];
+                    e1[2 * k + 1] = ob[k + 4];
+                }
+                Vec8<T>::store(y + ea, e0);
+                Vec8<T>::store(y + eb, e1);
+            } else {
+                Vec8<T>::store(y + ea, oa);
+                Vec8<T>::store(y + eb, ob);
+            }
+        };
+        if (is_q)
+            put(q_out + (t * hq + row) * D);
+        else
+            put((is_v ? vp : kp) + dst);
+    }
+}
+
 // One warp per (token, head) row of the output.
 __global__ void __launch_bounds__(256) kv_gather_kernel(
     const char* __restrict__ kp, const char* __restrict__ vp, PoolGeom g, int64_t layer,
@@ -527,6 +649,22 @@ int cx_kv_append_rope(const cx_pool* pool, int64_t layer, const void* k_new, con
         using S = decltype(s_tag);
         using P = decltype(p_tag);
         using QO = decltype(q_tag);
+        const uintptr_t al = reinterpret_cast<uintptr_t>(pool->k) |
+                             reinterpret_cast<uintptr_t>(pool->v) |
+                             reinterpret_cast<uintptr_t>(k_new) |
+                             reinterpret_cast<uintptr_t>(v_new) |
+                             reinterpret_cast<uintptr_t>(cos_table) |
+                             reinterpret_cast<uintptr_t>(sin_table) |
+                             reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(q_out);
+        if (pool->head_dim % 16 == 0 && (al & 15) == 0 &&
+            pool->n_blocks * pool->block_size < (1ll << 31)) {
+            kv_append_rope_vec_kernel<S, P, QO><<<grid_for(work / 8, 256), 256, 0, st>>>(
+                static_cast<P*>(pool->k), static_cast<P*>(pool->v), geom_of(pool), layer,
+                static_cast<const S*>(k_new), static_cast<const S*>(v_new), slot_mapping,
+                positions, n_tokens, cos_table, sin_table, table_rows, interleaved ? 1 : 0,
+                static_cast<const S*>(q), hq, static_cast<QO*>(q_out));
+            return check_launch("kv_append_rope_vec_kernel");
+        }
         kv_append_rope_kernel<S, P, QO><<<grid, 256, 0, st>>>(
             static_cast<P*>(pool->k), static_cast<P*>(pool->v), geom_of(pool), layer,
             static_cast<const S*>(k_new), static_cast<const S*>(v_new), slot_mapping, positions,

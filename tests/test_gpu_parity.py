@@ -467,6 +467,27 @@ def test_append_rope_matches_reference_apply_rope(name, pool_dtype):
     assert np.array_equal(q_bf.float().cpu().numpy(), bf16_round(want))
 
 
+@pytest.mark.parametrize("interleaved", [False, True])
+def test_append_rope_scalar_path_small_head_dim(interleaved):
+    """head_dim 12 (not a multiple of 16) takes the one-pair-per-thread kernel;
+    fp32 pool and Q output must equal the oracle's rotation bit for bit."""
+    from chenxing_b200 import RadixPagedKVCache, RopeTables
+    from oracle.rope import rotate
+    T, H, D = 37, 3, 12
+    rope = RopeTables(256, D, 10000.0, interleaved=interleaved)
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((T, H, D)).astype(np.float32)
+    pos = rng.integers(0, 256, size=T).astype(np.int64)
+    c = RadixPagedKVCache(4, 16, 1, H, D, dtype=np.float32, host_io=False)
+    slots = np.arange(T, dtype=np.int64)
+    q_out = c.append_rope(0, x, x, slots, pos, rope, q=x, q_out_dtype=torch.float32)
+    cos, sin = rope.cos.cpu().numpy(), rope.sin.cpu().numpy()
+    ref = rotate(x, cos, sin, pos, interleaved)
+    assert np.array_equal(q_out.cpu().numpy(), ref)
+    assert np.array_equal(c.k_pool[0].reshape(-1, H, D)[:T].cpu().numpy(), ref)
+    assert np.array_equal(c.v_pool[0].reshape(-1, H, D)[:T].cpu().numpy(), x)
+
+
 def test_append_rope_bf16_source_and_bad_position_flag():
     from chenxing_b200 import RadixPagedKVCache, _lib
     x, pos, want, rope = _rope_case("plain_hs")
