@@ -286,6 +286,22 @@ def test_prefill_tcgen05_matches_oracle(kw):
     case.check(case.run(batch), rtol=BF16_RTOL)
 
 
+@pytest.mark.parametrize("kw", [
+    dict(hq=32, hk=8, d=128, ctx=[300, 129, 64], q_lens=[16, 32, 64]),   # two query tiles
+    dict(hq=32, hk=8, d=128, ctx=[40], q_lens=[16]),                    # one query tile
+    dict(hq=32, hk=8, d=128, ctx=[1000, 777], q_lens=[200, 33], window=100),
+    dict(hq=32, hk=8, d=128, ctx=[900, 65]),                            # decode
+], ids=["tc-two-tiles", "tc-one-tile", "tc-window", "decode"])
+def test_negative_scale_matches_oracle(kw):
+    """A negative softmax scale (the tcgen05 kernels fold its sign into Q)
+    gives the attention of -Q at the default scale 1/sqrt(d)."""
+    case = PagedCase(seed=23, q_dtype=torch.bfloat16, **kw)
+    batch = case.batch(scale=-1.0 / np.sqrt(case.d))
+    out = case.run(batch)
+    case.q = -case.q                    # oracle side: exact for bf16 values
+    case.check(out, rtol=BF16_RTOL)
+
+
 def test_kernel_selection_by_packed_rows():
     """Decode and short verify chains (< 64 packed rows) stay on the split-K
     mma.sync kernel; 64 rows and more go to tcgen05; fp32 pools stay on the
