@@ -186,6 +186,17 @@ template <> struct QLoad<__nv_bfloat16> {
     }
 };
 
+// Rescale O only when a row max grows by more than 2^8 (see the consumer loop).
+constexpr float kMmaRescaleLog2 = 8.f;
+
+// 2^x as one special-function-unit instruction (ex2.approx.ftz: relative error
+// about 2^-22, far below the bf16 rounding of P; 2^-inf = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 template <int D, int MT, int HG>
 struct MmaCfg {
     static constexpr int KS = (HG * MT >= kConsumerWarps) ? 1 : kConsumerWarps / (HG * MT);
@@ -445,28 +456,36 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
                 mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
                 mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
                 mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-                const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+                // lazy rescale: a row keeps its reference max until its block
+                // max exceeds it by more than 2^8 (p <= 256 meanwhile; the
+                // final division, and the split-K merge, which uses each
+                // partial's own m, make a stale max exact)
+                const bool g0 = mx0 > m0 + kMmaRescaleLog2 || (m0 == -INFINITY && mx0 > -INFINITY);
+                const bool g1 = mx1 > m1 + kMmaRescaleLog2 || (m1 == -INFINITY && mx1 > -INFINITY);
+                const float mn0 = g0 ? mx0 : m0, mn1 = g1 ? mx1 : m1;
                 const float base0 = mn0 == -INFINITY ? 0.f : mn0;
                 const float base1 = mn1 == -INFINITY ? 0.f : mn1;
-                const float a0 = exp2f(m0 - base0), a1 = exp2f(m1 - base1);
+                const float a0 = g0 ? exp2f(m0 - base0) : 1.f, a1 = g1 ? exp2f(m1 - base1) : 1.f;
                 float pr[2][4];
 #pragma unroll
                 for (int n = 0; n < 2; ++n) {
-                    pr[n][0] = exp2f(x[n][0] - base0);
-                    pr[n][1] = exp2f(x[n][1] - base0);
-                    pr[n][2] = exp2f(x[n][2] - base1);
-                    pr[n][3] = exp2f(x[n][3] - base1);
+                    pr[n][0] = ex2_approx(x[n][0] - base0);
+                    pr[n][1] = ex2_approx(x[n][1] - base0);
+                    pr[n][2] = ex2_approx(x[n][2] - base1);
+                    pr[n][3] = ex2_approx(x[n][3] - base1);
                 }
                 l0 = l0 * a0 + (pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1]);
                 l1 = l1 * a1 + (pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3]);
                 m0 = mn0;
                 m1 = mn1;
+                if (__any_sync(0xffffffffu, g0 || g1)) {
 #pragma unroll
-                for (int n = 0; n < C::NT; ++n) {
-                    o[n][0] *= a0;
-                    o[n][1] *= a0;
-                    o[n][2] *= a1;
-                    o[n][3] *= a1;
+                    for (int n = 0; n < C::NT; ++n) {
+                        o[n][0] *= a0;
+                        o[n][1] *= a0;
+                        o[n][2] *= a1;
+                        o[n][3] *= a1;
+                    }
                 }
                 uint32_t pa[4];
                 pa[0] = pack_bf16(pr[0][0], pr[0][1]);
