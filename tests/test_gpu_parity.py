@@ -302,6 +302,25 @@ def test_negative_scale_matches_oracle(kw):
     case.check(out, rtol=BF16_RTOL)
 
 
+def test_tcgen05_row_max_jump_mid_sequence():
+    """Keys 512-639 (the fifth 128-key tile, visited after four ordinary ones)
+    scaled by 60 in the pool: their logits jump far past the rows' running
+    max, so the softmax must move its reference max and rescale O mid-row.
+    The oracle reads the same bf16 values back."""
+    from gpu_cases import pool_rows
+    case = PagedCase(seed=31, hq=32, hk=8, d=128, ctx=[1000], q_lens=[64],
+                     q_dtype=torch.bfloat16)
+    table = case.tables[0]
+    pos = torch.arange(512, 640, device="cuda")
+    bt = torch.as_tensor(table, dtype=torch.int64, device="cuda")[pos // case.bs]
+    case.cache._k[0, bt, :, pos % case.bs] *= 60
+    k, _ = pool_rows(case.cache, 0, table, 0, 1000)
+    case.k[:1000] = k
+    batch = case.batch()
+    assert batch.kernel_kind(case.q_dev.dtype) == "tcgen05"
+    case.check(case.run(batch), rtol=BF16_RTOL)
+
+
 def test_kernel_selection_by_packed_rows():
     """Decode and short verify chains (< 64 packed rows) stay on the split-K
     mma.sync kernel; 64 rows and more go to tcgen05; fp32 pools stay on the
