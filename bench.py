@@ -677,7 +677,7 @@ def run_prefill(args):
                        "attended_pairs_per_head": pairs,
                        "l2": "K/V > 126 MB L2" if kv_bytes > 126e6
                        else "K/V fits in L2 (small case)"},
-            "roofline": {"bound": "tensor", "kernel": "paged_attn_tc256_kernel" if D == 128 else "paged_attn_tc_kernel",
+            "roofline": {"bound": "tensor", "kernel": "paged_attn_tc256_kernel",
                          "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": tflops / peak, "peak_source": src,
                          "flops_per_launch": flops, "avg_launch_ms": avg,

@@ -812,10 +812,10 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
             return tiles_per_cta == 1
                        ? (q_dtype == CX_F32 ? launch_tc128<float>(tk, tv, t, st)
                                             : launch_tc128<__nv_bfloat16>(tk, tv, t, st))
-                       : (q_dtype == CX_F32 ? launch_tc256<float>(tk, tv, t, st)
-                                            : launch_tc256<__nv_bfloat16>(tk, tv, t, st));
-        return q_dtype == CX_F32 ? launch_tc<64, float>(tk, tv, t, st)
-                                 : launch_tc<64, __nv_bfloat16>(tk, tv, t, st);
+                       : (q_dtype == CX_F32 ? launch_tc256<128, float>(tk, tv, t, st)
+                                            : launch_tc256<128, __nv_bfloat16>(tk, tv, t, st));
+        return q_dtype == CX_F32 ? launch_tc256<64, float>(tk, tv, t, st)
+                                 : launch_tc256<64, __nv_bfloat16>(tk, tv, t, st);
     }
 
     if (!mma_eligible(pool, &b, q_dtype)) {

@@ -61,20 +61,21 @@ __device__ __forceinline__ void t128_item(int q, int n, bool& is_v, int& i) {
 }
 
 // TMA producer of the 128-key kernels (run by each of NPROD warps): ring items
-// (32 KB K or V tiles of eight 16-token pool blocks, two 128-byte swizzled
-// column halves each) in the order t128_item gives, key tile i + rot (mod
+// (K or V tiles of eight 16-token pool blocks, HALVES 128-byte swizzled 64-dim
+// column halves each: 16 KB per half) in the order t128_item gives, key tile i + rot (mod
 // n_tiles) for item tile i.  Producer pw loads blocks pw, pw + NPROD, ... of
 // each item.  The warps decide together at named barrier 1 whether an item goes
 // ahead, so an item is issued by all of them or by none and `s_issued` stays
 // exact for the teardown drain.
-template <int SLOTS, int NPROD>
+template <int SLOTS, int NPROD, int HALVES>
 __device__ __forceinline__ void t128_produce(const CUtensorMap* tmk, const CUtensorMap* tmv,
                                              const TcParams& p, int b, int h, int kb0,
                                              int nblk_seq, int n_tiles, int rot, int pw, int lane,
                                              unsigned char* ring, uint64_t* full, uint64_t* empty,
                                              volatile int* s_abort, volatile int* s_issued) {
     constexpr int BPT = kT128Keys / kBlockTok;              // 8 pool blocks per key tile
-    constexpr int SLOT = kT128Keys * 128 * 2;               // two 64-dim halves
+    constexpr int KV_HALF = kT128Keys * 128;                // one 64-dim half of a tile
+    constexpr int SLOT = KV_HALF * HALVES;
     const int32_t* tab = p.tables + (int64_t)b * p.table_stride;
     const int first_id = kb0 < nblk_seq ? tab[kb0] : 0;
     int my_blocks = 0;
@@ -119,8 +120,8 @@ __device__ __forceinline__ void t128_produce(const CUtensorMap* tmk, const CUten
             if (lane == 0) {
                 const int z = (p.layer * p.n_blocks + id) * p.hk + h;
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf)
-                    tma_load_3d(dst + hf * (SLOT / 2) + k * 2048, is_v ? tmv : tmk, &full[s],
+                for (int hf = 0; hf < HALVES; ++hf)
+                    tma_load_3d(dst + hf * KV_HALF + k * 2048, is_v ? tmv : tmk, &full[s],
                                 hf * 64, 0, z);
             }
         }
@@ -312,7 +313,7 @@ __global__ void __launch_bounds__(T128Cfg::THREADS, 1)
     }
 
     if (warp >= C::PRODUCER_WARP && warp < C::PRODUCER_WARP + C::N_PRODUCERS) {
-        t128_produce<kT128Slots, C::N_PRODUCERS>(&tmk, &tmv, p, b, h, kb0, nblk_seq, n_tiles, rot,
+        t128_produce<kT128Slots, C::N_PRODUCERS, 2>(&tmk, &tmv, p, b, h, kb0, nblk_seq, n_tiles, rot,
                                                  warp - C::PRODUCER_WARP, lane, ring, full,
                                                  empty, s_abort, s_issued);
     } else if (warp == C::MMA_WARP) {

@@ -1,5 +1,5 @@
-// Paged multi-query attention on tcgen05 for head_dim 128: two query tiles per
-// CTA and 128-key tiles (chunked prefill and long verify chains; used when a
+// Paged multi-query attention on tcgen05 for head_dim 64 or 128: two query
+// tiles per CTA and 128-key tiles (chunked prefill and long verify chains; used when a
 // sequence's packed query rows fill at least one 128-row tile).
 //
 // A K or V tile of 128 keys is read once for 256 query rows, half the load
@@ -12,11 +12,12 @@
 // 128 packed rows each (row r of tile w: token t0 + w * tpt + r / G, query head
 // h * G + r % G).  Twelve warps:
 //
-//   producer warps : t128_produce, three warps, a ring of five 32 KB slots
-//                    loaded in the order K(0), K(1), V(0), K(2), V(1), ... ;
+//   producer warps : t128_produce, three warps, a 160 KB ring of K or V tiles
+//                    (five slots of 32 KB at head_dim 128, ten of 16 KB at
+//                    64) loaded in the order K(0), K(1), V(0), K(2), V(1), ...;
 //   MMA warp       : one thread issues S_w(i) = Q_w K(i)^T into TMEM
 //                    [128 w, 128 w + 128) and O_w += P_w(i) V(i) into TMEM
-//                    [256 + 128 w, ...) with P_w read from TMEM, in the order
+//                    [256 + D w, ...) with P_w read from TMEM, in the order
 //                    PV_0(i), S_0(i+1), PV_1(i), S_1(i+1): while one tile's
 //                    softmax runs, the tensor pipe works on the other tile;
 //   warpgroup w    : softmax of query tile w, thread r owning row r (TMEM lane
@@ -34,7 +35,7 @@
 // no other wait before rescaling O_w or writing P_w(i), and S_w(i+1), issued
 // after PV_w(i), never overwrites a P that is still to be read.
 //
-// Q_0, Q_1 live in shared memory (32 KB each).  Every wait is
+// Q_0, Q_1 live in shared memory (D / 4 KB each).  Every wait is
 // bounded; on a timeout the CTA raises CX_DEV_WAIT_TIMEOUT, drains its own
 // copies and MMAs, frees its TMEM and returns.  tcgen05.ld / tcgen05.st are
 // warp-collective, so every branch around them is decided warp-uniformly.
@@ -43,7 +44,6 @@
 
 namespace cx {
 
-constexpr int kT256Slots = 5;    // ring slots, one K or V tile each
 
 // Ring position of K(j) and V(j) among n key tiles (the order t128_item gives).
 __device__ __forceinline__ int t128_pos_k(int j) { return j == 0 ? 0 : 2 * j - 1; }
@@ -51,30 +51,38 @@ __device__ __forceinline__ int t128_pos_v(int j, int n) {
     return n == 1 ? 1 : (j == n - 1 ? 2 * n - 1 : 2 * j + 2);
 }
 
+template <int D_>
 struct T256Cfg {
-    static constexpr int D = 128;
+    static constexpr int D = D_;
+    static constexpr int HALVES = D / 64;                   // 128-byte column halves
     static constexpr int Q_HALF = kTcRows * 128;            // 16 KB: 128 rows x 128 B
-    static constexpr int Q_BYTES = 2 * Q_HALF;              // one query tile
+    static constexpr int Q_BYTES = HALVES * Q_HALF;         // one query tile
     static constexpr int KV_HALF = kT128Keys * 128;         // 16 KB: 128 keys x 128 B
-    static constexpr int SLOT = 2 * KV_HALF;                // one K or V tile
+    static constexpr int SLOT = HALVES * KV_HALF;           // one K or V tile
+    static constexpr int SLOTS = 160 * 1024 / SLOT;         // ring of 160 KB
     static constexpr int OFF_Q = 0;                         // Q_0, Q_1
     static constexpr int OFF_RING = OFF_Q + 2 * Q_BYTES;
-    static constexpr int OFF_BAR = OFF_RING + kT256Slots * SLOT;
+    static constexpr int OFF_BAR = OFF_RING + SLOTS * SLOT;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;       // + 1 KB alignment slack
-    static constexpr int TMEM_COLS = 512;                   // S_0 / P_0, S_1 / P_1, O_0, O_1
+    // S_0 / P_0, S_1 / P_1, O_0, O_1 (256 + 2 D columns, allocated as 512)
+    static constexpr int TMEM_COLS = 512;
     static constexpr int N_PRODUCERS = 3;
     static constexpr int THREADS = 384;                     // softmax 2 x 4, producers 3, MMA
     static constexpr int PRODUCER_WARP = 8;                 // first producer warp
     static constexpr int MMA_WARP = 11;
 };
-static_assert(T256Cfg::SMEM <= 232448, "shared memory above the per-CTA limit");
+static_assert(T256Cfg<128>::SMEM <= 232448 && T256Cfg<64>::SMEM <= 232448,
+              "shared memory above the per-CTA limit");
+static_assert(T256Cfg<64>::SMEM > 232448 / 2, "one CTA per SM: its TMEM takes 512 columns");
+static_assert(T256Cfg<128>::SLOTS == 5 && T256Cfg<64>::SLOTS == 10, "ring depth");
 
-template <typename QT>
-__global__ void __launch_bounds__(T256Cfg::THREADS, 1)
+template <int DH, typename QT>
+__global__ void __launch_bounds__(T256Cfg<DH>::THREADS, 1)
     paged_attn_tc256_kernel(const __grid_constant__ CUtensorMap tmk,
                             const __grid_constant__ CUtensorMap tmv, const TcParams p) {
-    using C = T256Cfg;
+    using C = T256Cfg<DH>;
     constexpr int D = C::D;
+    constexpr int kT256Slots = C::SLOTS;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -197,7 +205,7 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
     }
 
     if (warp >= C::PRODUCER_WARP && warp < C::PRODUCER_WARP + C::N_PRODUCERS) {
-        t128_produce<kT256Slots, C::N_PRODUCERS>(&tmk, &tmv, p, b, h, kb0, nblk_seq, n_tiles, rot,
+        t128_produce<kT256Slots, C::N_PRODUCERS, C::HALVES>(&tmk, &tmv, p, b, h, kb0, nblk_seq, n_tiles, rot,
                                                  warp - C::PRODUCER_WARP, lane, ring, full,
                                                  empty, s_abort, s_issued);
     } else if (warp == C::MMA_WARP) {
@@ -442,11 +450,11 @@ __global__ void __launch_bounds__(T256Cfg::THREADS, 1)
                      : "memory");
 }
 
-template <typename QT>
+template <int DH, typename QT>
 static int launch_tc256(const CUtensorMap& tk, const CUtensorMap& tv, const TcParams& p,
                         cudaStream_t st) {
-    using C = T256Cfg;
-    auto kern = paged_attn_tc256_kernel<QT>;
+    using C = T256Cfg<DH>;
+    auto kern = paged_attn_tc256_kernel<DH, QT>;
     CX_CUDA_CHECK(
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     const int64_t grid = (int64_t)p.n_ctiles * p.batch * p.hk;
