@@ -45,12 +45,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["cfg2", "small", "prefill", "prefill-small", "append",
-                                         "cfg4", "copy"],
+    ap.add_argument("--config", choices=["cfg2", "small", "prefill", "prefill-small",
+                                         "prefill-d64", "append", "cfg4", "copy"],
                     default="cfg2",
                     help="small: 1 layer, pool sized to need (~2 GB, for profiler captures); "
                          "prefill: chunked-prefill attention on the tcgen05 kernel (its own "
                          "JSON line, TFLOP/s); prefill-small: the same, 2 sequences; "
+                         "prefill-d64: the same at head_dim 64; "
                          "append: prefill-sized KV append (its own JSON line, GB/s); "
                          "cfg4: speculative verify, gamma 4 and 8 (their own JSON lines); "
                          "copy: block copy (compaction) and read_layer gather (their own "
@@ -609,14 +610,15 @@ def run_prefill(args):
     """Chunked-prefill attention, one launch = one layer: B sequences each
     append a chunk of PREFILL_T tokens after ctx_prev ~ U[1024, 8192] cached
     ones and attend causally over ctx_prev + PREFILL_T keys (Hq 32 / Hkv 8,
-    D 128, bf16 pool, bf16 Q).  FLOPs per launch = 4 * Hq * D * sum over
-    sequences of attended (query, key) pairs."""
+    D 128, or 64 for prefill-d64; bf16 pool, bf16 Q).  FLOPs per launch =
+    4 * Hq * D * sum over sequences of attended (query, key) pairs."""
     import torch
     from chenxing_b200 import PagedBatch, RadixPagedKVCache, _lib
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    B = 8 if args.config == "prefill" else 2
+    B = 2 if args.config == "prefill-small" else 8
+    hd = 64 if args.config == "prefill-d64" else D        # head_dim of this mode
     rng = np.random.default_rng(args.seed)
     ctx_prev = rng.integers(1024, 8193, size=B).astype(np.int64)
     T = PREFILL_T
@@ -628,18 +630,18 @@ def run_prefill(args):
     for n in nb:
         tables.append([int(x) for x in perm[o:o + n]])
         o += n
-    cache = RadixPagedKVCache(n_blocks, BS, 1, HK, D, dtype="bfloat16", device=dev,
+    cache = RadixPagedKVCache(n_blocks, BS, 1, HK, hd, dtype="bfloat16", device=dev,
                               host_io=False)
     g = torch.Generator(device=dev)
     g.manual_seed(args.seed)
-    cache._k.normal_(0.0, 1.0 / math.sqrt(D), generator=g)
-    cache._v.normal_(0.0, 1.0 / math.sqrt(D), generator=g)
-    q = (torch.randn((B * T, HQ, D), device=dev, generator=g) / math.sqrt(D)).bfloat16()
-    out = torch.empty((B * T, HQ, D), dtype=torch.float32, device=dev)
+    cache._k.normal_(0.0, 1.0 / math.sqrt(hd), generator=g)
+    cache._v.normal_(0.0, 1.0 / math.sqrt(hd), generator=g)
+    q = (torch.randn((B * T, HQ, hd), device=dev, generator=g) / math.sqrt(hd)).bfloat16()
+    out = torch.empty((B * T, HQ, hd), dtype=torch.float32, device=dev)
     batch = PagedBatch(cache, tables, ctx, n_q_heads=HQ, q_lens=[T] * B)
     kind = batch.kernel_kind(q.dtype)
     pairs = int(sum(int(cp) * T + T * (T + 1) // 2 for cp in ctx_prev))
-    flops = 4.0 * HQ * D * pairs
+    flops = 4.0 * HQ * hd * pairs
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
         cache.verify_batch(0, q, batch, out)
@@ -666,14 +668,14 @@ def run_prefill(args):
             peak, src = float(json.load(f)["bf16_tflops"]), "measured (burst)"
     except (OSError, KeyError, ValueError):
         peak, src = 1590.0, "fallback"
-    kv_bytes = int(sum(int(c) for c in ctx)) * UNIT_BYTES     # one layer, K + V
+    kv_bytes = int(sum(int(c) for c in ctx)) * 2 * HK * hd * ELEM   # one layer, K + V
     line = {"metric": "chunked-prefill paged attention TFLOP/s (tcgen05 kernel)",
             "value": tflops, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": avg, "higher_is_better": True,
             "scaling": "none", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"chunked prefill: {B} sequences x {T}-token chunk after "
                                    f"ctx ~ U[1024, 8192]", "q_heads": HQ, "kv_heads": HK,
-                       "head_dim": D, "block_size": BS, "kernel": kind,
+                       "head_dim": hd, "block_size": BS, "kernel": kind,
                        "attended_pairs_per_head": pairs,
                        "l2": "K/V > 126 MB L2" if kv_bytes > 126e6
                        else "K/V fits in L2 (small case)"},
@@ -977,7 +979,7 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.config in ("prefill", "prefill-small"):
+    elif args.config in ("prefill", "prefill-small", "prefill-d64"):
         run_prefill(args)
     elif args.config == "append":
         run_append(args)
