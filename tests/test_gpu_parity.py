@@ -269,6 +269,8 @@ TC_CASES = [
     dict(hq=32, hk=8, d=128, ctx=[3000, 1500], q_lens=[1024, 300]),
     dict(hq=32, hk=8, d=128, ctx=[5000], q_lens=[257], window=4096),
     dict(hq=32, hk=8, d=64, ctx=[500, 90], q_lens=[70, 20]),
+    dict(hq=32, hk=8, d=64, ctx=[2000, 777], q_lens=[300, 40], window=200),
+    dict(hq=16, hk=4, d=64, ctx=[90], q_lens=[16], q_dtype=torch.bfloat16),
     dict(hq=8, hk=8, d=128, ctx=[700, 300], q_lens=[300, 64]),
     dict(hq=16, hk=8, d=128, ctx=[190, 33, 7], q_lens=[40, 33, 0]),
     dict(hq=64, hk=8, d=128, ctx=[260, 48], q_lens=[40, 8], q_dtype=torch.bfloat16),
@@ -291,7 +293,8 @@ def test_prefill_tcgen05_matches_oracle(kw):
     dict(hq=32, hk=8, d=128, ctx=[40], q_lens=[16]),                    # one query tile
     dict(hq=32, hk=8, d=128, ctx=[1000, 777], q_lens=[200, 33], window=100),
     dict(hq=32, hk=8, d=128, ctx=[900, 65]),                            # decode
-], ids=["tc-two-tiles", "tc-one-tile", "tc-window", "decode"])
+    dict(hq=32, hk=8, d=64, ctx=[600, 150], q_lens=[100, 40]),          # head_dim 64
+], ids=["tc-two-tiles", "tc-one-tile", "tc-window", "decode", "tc-d64"])
 def test_negative_scale_matches_oracle(kw):
     """A negative softmax scale (the tcgen05 kernels fold its sign into Q)
     gives the attention of -Q at the default scale 1/sqrt(d)."""
