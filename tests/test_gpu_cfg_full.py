@@ -93,7 +93,7 @@ def test_cfg4_full_size_verify_rollback_reverify(gamma):
             assert_close_rows(out[b * T:(b + 1) * T], ref, BF16_RTOL, f"seq {b}")
         return k_new, batch
 
-    # ---- round 1
+    # ---- first speculative verify step
     k1, batch1 = verify_round(ctx.astype(np.int64))
     assert batch1.kv_tokens == int(sum(min(int(c) + T, W + gamma) for c in ctx))
 
@@ -106,7 +106,7 @@ def test_cfg4_full_size_verify_rollback_reverify(gamma):
     assert np.array_equal(n_new, n_ref)
     tables_before = [list(t) for t in tables]
 
-    # ---- round 2: capacity growth bit-exact with the oracle, stale slots overwritten
+    # ---- second verify step: capacity growth bit-exact with the oracle, stale slots overwritten
     o_tables = [list(t) for t in tables]
     for b in range(B):
         grow_table(cache, tables[b], int(n_new[b]) + T)
