@@ -202,6 +202,9 @@ struct MmaCfg {
     static constexpr int KS = (HG * MT >= kConsumerWarps) ? 1 : kConsumerWarps / (HG * MT);
     static constexpr int NCW = HG * MT * KS;           // consumer warps
     static constexpr int THREADS = (NCW + 1) * 32;     // + producer warp
+    // units per consumer iteration: 2 when the block has at most 8 warps
+    // (two per SM sub-partition, so up to 255 registers a thread), else 1
+    static constexpr int U = NCW + 1 <= 8 ? 2 : 1;
     static constexpr int HALF_BOX = kBlockTok * 128;   // one head, 16 rows x 128 B
     static constexpr int TILES = HG * kBlockTok * D * 2;  // K (or V) bytes of a unit
     static constexpr int STAGE = 2 * TILES;
@@ -253,7 +256,10 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int B = p.batch, Hq = p.hq, G = p.group;
-    if (STAGES < 2 || STAGES % KS != 0) {
+    // A warp taking two units holds the first while it waits for the second
+    // (KS units later); the producer can fill that one only if the ring has
+    // more than KS stages.
+    if (STAGES < 2 || STAGES % KS != 0 || (C::U == 2 && STAGES < 2 * KS)) {
         if (tid == 0 && blockIdx.x == 0) raise_flag(CX_DEV_BAD_QLEN);
         return;
     }
@@ -402,11 +408,23 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
         for (int n = 0; n < C::NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
         float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
-        for (int k = ((ks - ibase) % KS + KS) % KS; k < seg.cnt; k += KS) {
-            const int i = ibase + k;
-            const int s = i % STAGES;
+        // U == 2: a warp takes two of its units per iteration (keys k and
+        // k + KS): twice the independent MMAs between waits and one softmax
+        // round (max, shuffles, vote) per 32 keys.
+        constexpr int U = C::U;
+        for (int k = ((ks - ibase) % KS + KS) % KS; k < seg.cnt; k += U * KS) {
+            const bool two = U == 2 && k + KS < seg.cnt;  // warp-uniform
+            int su[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) su[u] = (ibase + k + u * KS) % STAGES;
             bool ok = !*s_abort;
-            if (ok) ok = mbar_wait_bounded(&full_bar[s], (i / STAGES) & 1, s_abort, kWaitLimitNs);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = ibase + k + u * KS;
+                if (ok && (u == 0 || two))
+                    ok = mbar_wait_bounded(&full_bar[su[u]], (i / STAGES) & 1, s_abort,
+                                           kWaitLimitNs);
+            }
             // mma.sync / ldmatrix need the whole warp: agree on one outcome
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
@@ -415,43 +433,60 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
                     raise_flag(CX_DEV_WAIT_TIMEOUT);
                 }
             } else {
-                const uint32_t kb = smem_addr(ring + (size_t)s * C::STAGE);
-                const uint32_t vb = kb + C::TILES;
-                float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-                float sb[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                float x[U][2][4];
 #pragma unroll
-                for (int kk = 0; kk < C::KSTEP; ++kk) {
-                    uint32_t f[4];
-                    ldmatrix_x4(f, kb + C::swz(hh, k_tok, kk * 16 + k_dsub));
-                    if (kk & 1) {
-                        mma_bf16_16816(sb[0], qa[kk], f[0], f[1]);
-                        mma_bf16_16816(sb[1], qa[kk], f[2], f[3]);
-                    } else {
-                        mma_bf16_16816(sa[0], qa[kk], f[0], f[1]);
-                        mma_bf16_16816(sa[1], qa[kk], f[2], f[3]);
+                for (int u = 0; u < U; ++u) {
+                    if (u > 0 && !two) {
+#pragma unroll
+                        for (int n = 0; n < 2; ++n)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) x[u][n][e] = -INFINITY;
+                        continue;
                     }
-                }
-                float x[2][4];
+                    const uint32_t kb = smem_addr(ring + (size_t)su[u] * C::STAGE);
+                    float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                    float sb[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-                for (int n = 0; n < 2; ++n)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) x[n][e] = (sa[n][e] + sb[n][e]) * p.scale_log2;
-                const int t0 = (seg.j0 + k) * kBlockTok;
-                const bool edge = (t0 + kBlockTok - 1 > pos0) ||
-                                  (p.window > 0 && t0 <= ctx - 1 - p.window);
-                if (edge) {
+                    for (int kk = 0; kk < C::KSTEP; ++kk) {
+                        uint32_t f[4];
+                        ldmatrix_x4(f, kb + C::swz(hh, k_tok, kk * 16 + k_dsub));
+                        if (kk & 1) {
+                            mma_bf16_16816(sb[0], qa[kk], f[0], f[1]);
+                            mma_bf16_16816(sb[1], qa[kk], f[2], f[3]);
+                        } else {
+                            mma_bf16_16816(sa[0], qa[kk], f[0], f[1]);
+                            mma_bf16_16816(sa[1], qa[kk], f[2], f[3]);
+                        }
+                    }
 #pragma unroll
                     for (int n = 0; n < 2; ++n)
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int tok = t0 + n * 8 + qc + (e & 1);
-                            const int rp = (e < 2) ? rpos0 : rpos1;
-                            const bool ok_t = tok <= rp && (p.window <= 0 || tok > rp - p.window);
-                            if (!ok_t) x[n][e] = -INFINITY;
-                        }
+                        for (int e = 0; e < 4; ++e)
+                            x[u][n][e] = (sa[n][e] + sb[n][e]) * p.scale_log2;
+                    const int t0 = (seg.j0 + k + u * KS) * kBlockTok;
+                    const bool edge = (t0 + kBlockTok - 1 > pos0) ||
+                                      (p.window > 0 && t0 <= ctx - 1 - p.window);
+                    if (edge) {
+#pragma unroll
+                        for (int n = 0; n < 2; ++n)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int tok = t0 + n * 8 + qc + (e & 1);
+                                const int rp = (e < 2) ? rpos0 : rpos1;
+                                const bool ok_t =
+                                    tok <= rp && (p.window <= 0 || tok > rp - p.window);
+                                if (!ok_t) x[u][n][e] = -INFINITY;
+                            }
+                    }
                 }
-                float mx0 = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
-                float mx1 = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
+                float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    mx0 = fmaxf(mx0, fmaxf(fmaxf(x[u][0][0], x[u][0][1]),
+                                           fmaxf(x[u][1][0], x[u][1][1])));
+                    mx1 = fmaxf(mx1, fmaxf(fmaxf(x[u][0][2], x[u][0][3]),
+                                           fmaxf(x[u][1][2], x[u][1][3])));
+                }
                 mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
                 mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
                 mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
@@ -466,16 +501,24 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
                 const float base0 = mn0 == -INFINITY ? 0.f : mn0;
                 const float base1 = mn1 == -INFINITY ? 0.f : mn1;
                 const float a0 = g0 ? exp2f(m0 - base0) : 1.f, a1 = g1 ? exp2f(m1 - base1) : 1.f;
-                float pr[2][4];
+                float pr[U][2][4];
+                float r0, r1;
 #pragma unroll
-                for (int n = 0; n < 2; ++n) {
-                    pr[n][0] = ex2_approx(x[n][0] - base0);
-                    pr[n][1] = ex2_approx(x[n][1] - base0);
-                    pr[n][2] = ex2_approx(x[n][2] - base1);
-                    pr[n][3] = ex2_approx(x[n][3] - base1);
+                for (int u = 0; u < U; ++u) {
+#pragma unroll
+                    for (int n = 0; n < 2; ++n) {
+                        pr[u][n][0] = ex2_approx(x[u][n][0] - base0);
+                        pr[u][n][1] = ex2_approx(x[u][n][1] - base0);
+                        pr[u][n][2] = ex2_approx(x[u][n][2] - base1);
+                        pr[u][n][3] = ex2_approx(x[u][n][3] - base1);
+                    }
+                    const float q0 = pr[u][0][0] + pr[u][0][1] + pr[u][1][0] + pr[u][1][1];
+                    const float q1 = pr[u][0][2] + pr[u][0][3] + pr[u][1][2] + pr[u][1][3];
+                    r0 = u == 0 ? q0 : r0 + q0;
+                    r1 = u == 0 ? q1 : r1 + q1;
                 }
-                l0 = l0 * a0 + (pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1]);
-                l1 = l1 * a1 + (pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3]);
+                l0 = l0 * a0 + r0;
+                l1 = l1 * a1 + r1;
                 m0 = mn0;
                 m1 = mn1;
                 if (__any_sync(0xffffffffu, g0 || g1)) {
@@ -487,21 +530,29 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
                         o[n][3] *= a1;
                     }
                 }
-                uint32_t pa[4];
-                pa[0] = pack_bf16(pr[0][0], pr[0][1]);
-                pa[1] = pack_bf16(pr[0][2], pr[0][3]);
-                pa[2] = pack_bf16(pr[1][0], pr[1][1]);
-                pa[3] = pack_bf16(pr[1][2], pr[1][3]);
 #pragma unroll
-                for (int np = 0; np < C::KSTEP; ++np) {
-                    uint32_t f[4];
-                    ldmatrix_x4_trans(f, vb + C::swz(hh, v_tok, np * 16 + v_dsub));
-                    mma_bf16_16816(o[2 * np], pa, f[0], f[1]);
-                    mma_bf16_16816(o[2 * np + 1], pa, f[2], f[3]);
+                for (int u = 0; u < U; ++u) {
+                    if (u > 0 && !two) continue;
+                    const uint32_t vb = smem_addr(ring + (size_t)su[u] * C::STAGE) + C::TILES;
+                    uint32_t pa[4];
+                    pa[0] = pack_bf16(pr[u][0][0], pr[u][0][1]);
+                    pa[1] = pack_bf16(pr[u][0][2], pr[u][0][3]);
+                    pa[2] = pack_bf16(pr[u][1][0], pr[u][1][1]);
+                    pa[3] = pack_bf16(pr[u][1][2], pr[u][1][3]);
+#pragma unroll
+                    for (int np = 0; np < C::KSTEP; ++np) {
+                        uint32_t f[4];
+                        ldmatrix_x4_trans(f, vb + C::swz(hh, v_tok, np * 16 + v_dsub));
+                        mma_bf16_16816(o[2 * np], pa, f[0], f[1]);
+                        mma_bf16_16816(o[2 * np + 1], pa, f[2], f[3]);
+                    }
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty_bar[s]);
+            if (lane == 0) {
+                mbar_arrive(&empty_bar[su[0]]);
+                if (two) mbar_arrive(&empty_bar[su[U - 1]]);
+            }
         }
         ibase += seg.cnt;
 
@@ -722,7 +773,7 @@ static int launch_mma_cfg(const CUtensorMap& tk, const CUtensorMap& tv, MmaParam
     auto kern = paged_attn_mma_kernel<D, MT, HG, QT>;
     p.stages = C::stages_for(p.rows);
     p.stage_bytes = C::STAGE;
-    if (p.stages < 2 || p.stages % C::KS != 0)
+    if (p.stages < 2 || p.stages % C::KS != 0 || (C::U == 2 && p.stages < 2 * C::KS))
         return fail(CX_ERR_UNSUPPORTED, "paged attention: shared memory too small");
     const size_t smem = C::smem_bytes(p.rows, p.stages);
     CX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -258,6 +258,26 @@ def test_verify_ragged_query_lengths():
     case.check(case.run(), rtol=BF16_RTOL)
 
 
+# 33-48 packed rows per KV head: three row tiles, each consumer warp takes two
+# of its blocks per iteration (odd and even block counts, ranges cut across
+# CTAs, one head per unit with two key slices, head_dim 64, windows)
+PAIRED_CASES = [
+    dict(hq=12, hk=3, d=128, ctx=[20000, 37, 16, 1500, 9], q_lens=[9, 12, 10, 11, 9]),
+    dict(hq=32, hk=8, d=64, ctx=[9000, 100, 33, 2048], q_lens=[9] * 4, window=300),
+    dict(hq=32, hk=8, d=128, ctx=[20000, 3000, 17], q_lens=[9, 9, 9],
+         q_dtype=torch.bfloat16),
+    dict(hq=32, hk=8, d=128, ctx=[4096, 4097, 33, 48], q_lens=[12, 9, 10, 12], window=4096),
+]
+
+
+@pytest.mark.parametrize("kw", PAIRED_CASES, ids=lambda kw: "-".join(
+    f"{k}{v}" for k, v in kw.items() if k in ("hq", "hk", "d", "window")))
+def test_verify_three_row_tiles_matches_oracle(kw):
+    case = PagedCase(seed=41, **kw)
+    assert case.batch().kernel_kind() == "mma"
+    case.check(case.run(), rtol=BF16_RTOL)
+
+
 # ---------------------------------------------------------------------------
 # packed query tiles of >= 64 rows: the tcgen05 / TMEM kernel (chunked
 # prefill and long verify chains)
