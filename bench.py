@@ -46,7 +46,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["cfg2", "small", "prefill", "prefill-small",
-                                         "prefill-d64", "append", "cfg4", "copy"],
+                                         "prefill-d64", "append", "cfg4", "cfg4-small",
+                                         "copy"],
                     default="cfg2",
                     help="small: 1 layer, pool sized to need (~2 GB, for profiler captures); "
                          "prefill: chunked-prefill attention on the tcgen05 kernel (its own "
@@ -54,6 +55,8 @@ def parse():
                          "prefill-d64: the same at head_dim 64; "
                          "append: prefill-sized KV append (its own JSON line, GB/s); "
                          "cfg4: speculative verify, gamma 4 and 8 (their own JSON lines); "
+                         "cfg4-small: the same with 16 sequences (~2.4 GB, for profiler "
+                         "captures); "
                          "copy: block copy (compaction) and read_layer gather (their own "
                          "JSON lines, GB/s)")
     ap.add_argument("--pool-frac", type=float, default=0.9)
@@ -61,6 +64,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--gamma", type=int, choices=[0, 4, 8], default=0,
+                    help="cfg4 / cfg4-small: draft length to run (0: both 4 and 8)")
     return ap.parse_args()
 
 
@@ -881,7 +886,7 @@ def run_copy(args):
 # cfg4: speculative verify (separate mode, not the headline)
 # ---------------------------------------------------------------------------
 def run_verify(args):
-    """cfg4: 128 sequences, ctx ~ U[2048, 16384], gamma + 1 query tokens each
+    """cfg4: 128 sequences (cfg4-small: 16), ctx ~ U[2048, 16384], gamma + 1 query tokens each
     (causal within the draft), 4096-token sliding window, Hq 32 / Hkv 8,
     D 128, bf16.  One step = for each of 4 layers: append the gamma + 1 K/V
     rows per sequence, then verify attention.  Units = windowed keys
@@ -893,9 +898,9 @@ def run_verify(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    B, W, layers = 128, 4096, 4
+    B, W, layers = (16 if args.config == "cfg4-small" else 128), 4096, 4
     peak, kind = measured_peak()
-    for gamma in (4, 8):
+    for gamma in ((args.gamma,) if args.gamma else (4, 8)):
         T = gamma + 1
         ctx = np.random.default_rng(args.seed).integers(2048, 16385, size=B)
         n_blocks = int(sum(-(-(int(c) + T) // BS) for c in ctx)) + 64
@@ -983,7 +988,7 @@ def main():
         run_prefill(args)
     elif args.config == "append":
         run_append(args)
-    elif args.config == "cfg4":
+    elif args.config in ("cfg4", "cfg4-small"):
         run_verify(args)
     elif args.config == "copy":
         run_copy(args)

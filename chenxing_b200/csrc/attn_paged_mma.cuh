@@ -205,6 +205,11 @@ struct MmaCfg {
     // units per consumer iteration: 2 when the block has at most 8 warps
     // (two per SM sub-partition, so up to 255 registers a thread), else 1
     static constexpr int U = NCW + 1 <= 8 ? 2 : 1;
+    // Q fragments in shared memory (one 16-byte slot per lane and k-step,
+    // reloaded per block) instead of registers: lets 12 consumer warps (13
+    // warps, 128 registers a thread) run without spilling
+    static constexpr bool QSM = NCW + 1 > 12;
+    static constexpr size_t QSM_BYTES = QSM ? (size_t)NCW * (D / 16) * 32 * 16 : 0;
     static constexpr int HALF_BOX = kBlockTok * 128;   // one head, 16 rows x 128 B
     static constexpr int TILES = HG * kBlockTok * D * 2;  // K (or V) bytes of a unit
     static constexpr int STAGE = 2 * TILES;
@@ -220,7 +225,7 @@ struct MmaCfg {
         return KS > 1 ? (size_t)KS * HG * rows * (D + 2) * sizeof(float) : 0;
     }
     static int stages_for(int rows) {
-        const size_t fixed = 1024 + merge_bytes(rows) + 64;
+        const size_t fixed = 1024 + merge_bytes(rows) + 64 + QSM_BYTES;
         const size_t avail = kSmemBudget > fixed ? kSmemBudget - fixed : 0;
         int s = (int)(avail / (STAGE + 2 * sizeof(uint64_t)));
         s = s > 32 ? 32 : s;
@@ -232,7 +237,7 @@ struct MmaCfg {
     }
     static size_t smem_bytes(int rows, int stages) {
         return 1024 + (size_t)stages * STAGE + 2 * stages * sizeof(uint64_t) + merge_bytes(rows) +
-               64;
+               64 + QSM_BYTES;
     }
 };
 
@@ -368,6 +373,9 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
     const int qr0 = lane >> 2, qc = 2 * (lane & 3);
     const int R0 = mt * 16 + qr0, R1 = R0 + 8;  // packed rows this lane owns
     const QT* qbase = static_cast<const QT*>(p.q);
+    // this lane's Q slots when C::QSM: [warp][k-step][lane] x 16 B after the flags
+    const uint32_t q_slot = smem_addr(reinterpret_cast<unsigned char*>(s_flags) + 64) +
+                            (uint32_t)((warp * C::KSTEP * 32 + lane) * 16);
     const size_t slot_floats = (size_t)HG * p.rows * (D + 2);
 
     int ibase = 0;
@@ -401,6 +409,12 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
             qa[kk][1] = pack_bf16(bq.x, bq.y);
             qa[kk][2] = pack_bf16(c.x, c.y);
             qa[kk][3] = pack_bf16(d.x, d.y);
+        }
+        if constexpr (C::QSM) {
+            // each lane writes and later reads only its own slots
+#pragma unroll
+            for (int kk = 0; kk < C::KSTEP; ++kk)
+                st_shared_v4(q_slot + kk * 32 * 16, qa[kk]);
         }
 
         float o[C::NT][4];
@@ -450,12 +464,21 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
                     for (int kk = 0; kk < C::KSTEP; ++kk) {
                         uint32_t f[4];
                         ldmatrix_x4(f, kb + C::swz(hh, k_tok, kk * 16 + k_dsub));
-                        if (kk & 1) {
-                            mma_bf16_16816(sb[0], qa[kk], f[0], f[1]);
-                            mma_bf16_16816(sb[1], qa[kk], f[2], f[3]);
+                        uint32_t qk[4];
+                        if constexpr (C::QSM) {
+                            ld_shared_v4(qk, q_slot + kk * 32 * 16);
                         } else {
-                            mma_bf16_16816(sa[0], qa[kk], f[0], f[1]);
-                            mma_bf16_16816(sa[1], qa[kk], f[2], f[3]);
+                            qk[0] = qa[kk][0];
+                            qk[1] = qa[kk][1];
+                            qk[2] = qa[kk][2];
+                            qk[3] = qa[kk][3];
+                        }
+                        if (kk & 1) {
+                            mma_bf16_16816(sb[0], qk, f[0], f[1]);
+                            mma_bf16_16816(sb[1], qk, f[2], f[3]);
+                        } else {
+                            mma_bf16_16816(sa[0], qk, f[0], f[1]);
+                            mma_bf16_16816(sa[1], qk, f[2], f[3]);
                         }
                     }
 #pragma unroll
@@ -733,15 +756,16 @@ struct MmaShape {
 };
 
 // Heads per unit: a power of two dividing the KV head count, at most 4 (one
-// or two row tiles) or 2 (more): 4 heads keep a unit's 16-token stage at 32 KB
-// (8 KB TMA boxes), so the ring has six stages and frees them in finer steps;
-// 8 heads (64 KB stages, three of them) measured 2.7 % slower at decode, 2
-// heads (4 KB boxes) 16 % slower.  The row-tile warps are then split over
-// the unit's blocks (ks) up to 8 consumer warps.
+// to three row tiles) or 2 (four): 4 heads keep a unit's 16-token stage at
+// 32 KB (8 KB TMA boxes), so the ring has six stages and frees them in finer
+// steps; 8 heads (64 KB stages, three of them) measured 2.7 % slower at
+// decode, 2 heads (4 KB boxes) 16 % slower.  The row-tile warps are then
+// split over the unit's blocks (ks) up to 8 consumer warps; three row tiles
+// of 4 heads run 12 consumer warps with Q in shared memory (MmaCfg::QSM).
 static MmaShape mma_shape(int64_t hk, int64_t rows) {
     MmaShape s{};
     s.mt = (int)((rows + 15) / 16);
-    const int cap = s.mt <= 2 ? 4 : 2;
+    const int cap = s.mt <= 3 ? 4 : 2;
     s.hg = 1;
     while (s.hg * 2 <= cap && hk % (s.hg * 2) == 0) s.hg *= 2;
     s.ks = s.hg * s.mt >= kConsumerWarps ? 1 : kConsumerWarps / (s.hg * s.mt);
@@ -788,7 +812,7 @@ static int launch_mma_d(const MmaShape& sh, const CUtensorMap& tk, const CUtenso
     if (sh.mt == MT_ && sh.hg == HG_) return launch_mma_cfg<D, MT_, HG_, QT>(tk, tv, p, st, grid);
     CX_CASE(1, 8) CX_CASE(1, 4) CX_CASE(1, 2) CX_CASE(1, 1)
     CX_CASE(2, 4) CX_CASE(2, 2) CX_CASE(2, 1)
-    CX_CASE(3, 2) CX_CASE(3, 1)
+    CX_CASE(3, 4) CX_CASE(3, 2) CX_CASE(3, 1)
     CX_CASE(4, 2) CX_CASE(4, 1)
 #undef CX_CASE
     return fail(CX_ERR_UNSUPPORTED, "paged attention: no kernel for this row/head shape");

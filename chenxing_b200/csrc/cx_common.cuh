@@ -137,6 +137,21 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
         : "memory");
 }
 
+// 16-byte shared-memory store / load of four words.  The load is volatile so
+// that it stays where it is written (inside a loop) instead of being hoisted
+// into registers.
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, const uint32_t (&r)[4]) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+}
+
+__device__ __forceinline__ void ld_shared_v4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
 __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])

@@ -258,11 +258,14 @@ def test_verify_ragged_query_lengths():
     case.check(case.run(), rtol=BF16_RTOL)
 
 
-# 33-48 packed rows per KV head: three row tiles, each consumer warp takes two
-# of its blocks per iteration (odd and even block counts, ranges cut across
-# CTAs, one head per unit with two key slices, head_dim 64, windows)
+# 33-48 packed rows per KV head: three row tiles.  4 heads per unit (12
+# consumer warps, Q fragments reloaded from shared memory), or 2 / 1 heads
+# per unit with each consumer warp taking two of its blocks per iteration
+# (odd and even block counts, ranges cut across CTAs, two key slices), head
+# dims 128 and 64, windows
 PAIRED_CASES = [
     dict(hq=12, hk=3, d=128, ctx=[20000, 37, 16, 1500, 9], q_lens=[9, 12, 10, 11, 9]),
+    dict(hq=8, hk=2, d=128, ctx=[9000, 33, 700, 16], q_lens=[9, 12, 9, 10], window=512),
     dict(hq=32, hk=8, d=64, ctx=[9000, 100, 33, 2048], q_lens=[9] * 4, window=300),
     dict(hq=32, hk=8, d=128, ctx=[20000, 3000, 17], q_lens=[9, 9, 9],
          q_dtype=torch.bfloat16),
