@@ -202,13 +202,16 @@ struct MmaCfg {
     static constexpr int KS = (HG * MT >= kConsumerWarps) ? 1 : kConsumerWarps / (HG * MT);
     static constexpr int NCW = HG * MT * KS;           // consumer warps
     static constexpr int THREADS = (NCW + 1) * 32;     // + producer warp
-    // units per consumer iteration: 2 when the block has at most 8 warps
-    // (two per SM sub-partition, so up to 255 registers a thread), else 1
-    static constexpr int U = NCW + 1 <= 8 ? 2 : 1;
     // Q fragments in shared memory (one 16-byte slot per lane and k-step,
     // reloaded per block) instead of registers: lets 12 consumer warps (13
-    // warps, 128 registers a thread) run without spilling
-    static constexpr bool QSM = NCW + 1 > 12;
+    // warps, 128 registers a thread) run without spilling, and frees the
+    // registers for two blocks per iteration at two row tiles.  Decode (one
+    // row tile) keeps Q in registers: the slots would cost it two ring stages.
+    static constexpr bool QSM = NCW + 1 > 12 || MT == 2;
+    // blocks per consumer iteration: 2 when the block has at most 8 warps (two
+    // per SM sub-partition, so up to 255 registers a thread) or Q sits in
+    // shared memory at two row tiles, else 1
+    static constexpr int U = (NCW + 1 <= 8 || MT == 2) ? 2 : 1;
     static constexpr size_t QSM_BYTES = QSM ? (size_t)NCW * (D / 16) * 32 * 16 : 0;
     static constexpr int HALF_BOX = kBlockTok * 128;   // one head, 16 rows x 128 B
     static constexpr int TILES = HG * kBlockTok * D * 2;  // K (or V) bytes of a unit

@@ -258,12 +258,15 @@ def test_verify_ragged_query_lengths():
     case.check(case.run(), rtol=BF16_RTOL)
 
 
-# 33-48 packed rows per KV head: three row tiles.  4 heads per unit (12
-# consumer warps, Q fragments reloaded from shared memory), or 2 / 1 heads
-# per unit with each consumer warp taking two of its blocks per iteration
-# (odd and even block counts, ranges cut across CTAs, two key slices), head
-# dims 128 and 64, windows
+# 17-48 packed rows per KV head: two or three row tiles, every consumer warp
+# taking two of its blocks per iteration (odd and even block counts, ranges
+# cut across CTAs, key slices), Q fragments reloaded from shared memory at two
+# row tiles and at three tiles of 4 heads (12 consumer warps); 4 / 2 / 1
+# heads per unit, head dims 128 and 64, windows
 PAIRED_CASES = [
+    dict(hq=8, hk=2, d=128, ctx=[7000, 21, 300, 16], q_lens=[5, 8, 6, 5]),
+    dict(hq=12, hk=3, d=64, ctx=[12000, 99, 8, 2049], q_lens=[8, 5, 7, 6], window=1000),
+    dict(hq=32, hk=8, d=128, ctx=[16000, 5000, 9], q_lens=[5, 8, 5], q_dtype=torch.bfloat16),
     dict(hq=12, hk=3, d=128, ctx=[20000, 37, 16, 1500, 9], q_lens=[9, 12, 10, 11, 9]),
     dict(hq=8, hk=2, d=128, ctx=[9000, 33, 700, 16], q_lens=[9, 12, 9, 10], window=512),
     dict(hq=32, hk=8, d=64, ctx=[9000, 100, 33, 2048], q_lens=[9] * 4, window=300),
@@ -275,7 +278,7 @@ PAIRED_CASES = [
 
 @pytest.mark.parametrize("kw", PAIRED_CASES, ids=lambda kw: "-".join(
     f"{k}{v}" for k, v in kw.items() if k in ("hq", "hk", "d", "window")))
-def test_verify_three_row_tiles_matches_oracle(kw):
+def test_verify_row_tiles_two_blocks_per_iteration(kw):
     case = PagedCase(seed=41, **kw)
     assert case.batch().kernel_kind() == "mma"
     case.check(case.run(), rtol=BF16_RTOL)
