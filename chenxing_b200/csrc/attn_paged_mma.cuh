@@ -684,25 +684,34 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
             if (last) {
                 __threadfence();
                 const int pf = (last - 1) & 0xffff, pl = (last - 1) >> 16;
-                for (int e = ctid; e < HG * rows_b * D; e += NCT) {
-                    const int d = e % D;
-                    const int R = (e / D) % rows_b;
-                    const int eh = e / (D * rows_b);
-                    const size_t roff = ((size_t)eh * p.rows + R) * (D + 2);
-                    float M = -INFINITY;
-                    for (int pp = pf; pp <= pl; ++pp)
-                        M = fmaxf(M, __ldcg(p.partials + (size_t)(pp + bg) * slot_floats + roff + D));
-                    float L = 0.f, O = 0.f;
-                    if (M != -INFINITY) {
-                        for (int pp = pf; pp <= pl; ++pp) {
-                            const float* r = p.partials + (size_t)(pp + bg) * slot_floats + roff;
-                            const float wgt = exp2f(__ldcg(r + D) - M);
-                            L += __ldcg(r + D + 1) * wgt;
-                            O += __ldcg(r + d) * wgt;
-                        }
+                // one pass over the partials, two columns per thread: the loads
+                // of every partial are independent of the running merge, so
+                // they overlap instead of costing an L2 round trip each
+                constexpr int D2 = D / 2;
+                for (int e = ctid; e < HG * rows_b * D2; e += NCT) {
+                    const int d = 2 * (e % D2);
+                    const int R = (e / D2) % rows_b;
+                    const int eh = e / (D2 * rows_b);
+                    const float* r0 = p.partials + (size_t)(pf + bg) * slot_floats +
+                                      ((size_t)eh * p.rows + R) * (D + 2);
+                    float M = -INFINITY, L = 0.f, Ox = 0.f, Oy = 0.f;
+#pragma unroll 4
+                    for (int pp = 0; pp <= pl - pf; ++pp) {
+                        const float* r = r0 + (size_t)pp * slot_floats;
+                        const float m = __ldcg(r + D), l = __ldcg(r + D + 1);
+                        const float2 o = __ldcg(reinterpret_cast<const float2*>(r + d));
+                        if (m == -INFINITY) continue;  // a partial that saw no key
+                        const float Mn = fmaxf(M, m);
+                        const float a = exp2f(M - Mn), w = exp2f(m - Mn);
+                        L = L * a + l * w;
+                        Ox = Ox * a + o.x * w;
+                        Oy = Oy * a + o.y * w;
+                        M = Mn;
                     }
                     const int64_t orow = (qs + R / G) * Hq + (int64_t)(seg.g * HG + eh) * G + R % G;
-                    p.out[orow * D + d] = L > 0.f ? O / L : 0.f;
+                    const float inv = L > 0.f ? 1.f / L : 0.f;
+                    *reinterpret_cast<float2*>(p.out + orow * D + d) =
+                        L > 0.f ? make_float2(Ox * inv, Oy * inv) : make_float2(0.f, 0.f);
                 }
                 if (ctid == 0) p.counters[bg] = 0;
             }
@@ -858,7 +867,10 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
     cx_attn_batch b = *bt;
     b.max_q_len = max_q;
 
-    if (tc_eligible(pool, &b, q_dtype)) {
+    // The tensor-core kernels move Q and the output rows with 8- and 16-byte
+    // vector accesses; other pointers take the element-wise generic kernel.
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+    if (vec_ok && tc_eligible(pool, &b, q_dtype)) {
         // packed query tile >= 64 rows: tcgen05 kernel, no workspace
         const int G = (int)(b.n_q_heads / pool->n_kv_heads);
         TcParams t{};
@@ -900,7 +912,7 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
                                  : launch_tc256<64, __nv_bfloat16>(tk, tv, t, st);
     }
 
-    if (!mma_eligible(pool, &b, q_dtype)) {
+    if (!vec_ok || !mma_eligible(pool, &b, q_dtype)) {
         GenericParams g{};
         g.q = q;
         g.out = out;

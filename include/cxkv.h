@@ -199,7 +199,9 @@ int cx_paged_decode_static(const cx_pool* pool, int64_t layer, const cx_attn_bat
  * block sizes or head dims: exact CUDA-core kernel), CX_KERNEL_MMA (bf16
  * pool, packed query tile of 1..63 rows: TMA + mma.sync split-K kernel) or
  * CX_KERNEL_TCGEN05 (bf16 pool, packed tile of 64 rows or more: TMA +
- * tcgen05 / TMEM kernel).  Reads only the host fields of `batch`. */
+ * tcgen05 / TMEM kernel).  Reads only the host fields of `batch` and assumes
+ * 16-byte-aligned q and out pointers: the decode / verify calls run the
+ * generic kernel for q or out pointers that are not 16-byte aligned. */
 enum { CX_KERNEL_GENERIC = 0, CX_KERNEL_MMA = 1, CX_KERNEL_TCGEN05 = 2 };
 int cx_paged_kernel_kind(const cx_pool* pool, const cx_attn_batch* batch, int32_t q_dtype,
                          int32_t verify);

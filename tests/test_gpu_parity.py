@@ -276,6 +276,24 @@ PAIRED_CASES = [
 ]
 
 
+@pytest.mark.parametrize("q_lens", [[9, 9], [16, 20]], ids=["mma-shape", "tcgen05-shape"])
+def test_unaligned_q_and_out_take_the_generic_kernel(q_lens):
+    """q / out views 4 bytes past a 16-byte boundary: the tensor-core kernels
+    move them with vector accesses, so the call runs the element-wise kernel
+    and still matches the oracle."""
+    case = PagedCase(hq=32, hk=8, d=128, ctx=[300, 1000], q_lens=q_lens, seed=19)
+    n = case.q_dev.numel()
+    qbuf = torch.zeros(n + 4, dtype=torch.float32, device="cuda")
+    qbuf[1:n + 1] = case.q_dev.reshape(-1)
+    q = qbuf[1:n + 1].view(case.q_dev.shape)
+    obuf = torch.full((n + 4,), float("nan"), dtype=torch.float32, device="cuda")
+    out = obuf[1:n + 1].view(case.q_dev.shape)
+    assert q.data_ptr() % 16 == 4 and out.data_ptr() % 16 == 4
+    case.cache.verify_batch(0, q, case.batch(), out=out)
+    torch.cuda.synchronize()
+    case.check(out.cpu().numpy(), rtol=BF16_RTOL)
+
+
 @pytest.mark.parametrize("kw", PAIRED_CASES, ids=lambda kw: "-".join(
     f"{k}{v}" for k, v in kw.items() if k in ("hq", "hk", "d", "window")))
 def test_verify_row_tiles_two_blocks_per_iteration(kw):
