@@ -13,7 +13,8 @@
 // may start or end inside a (sequence, head group) range; such a range is
 // finished by whichever CTA arrives last at its counter (atomic ticket, no
 // waiting), which merges the per-CTA partial softmax states from the
-// workspace (log-sum-exp merge) and writes the final rows.
+// workspace (log-sum-exp merge, one pass over the partials) and writes the
+// final rows.
 //
 // Inside a CTA: the last warp is the producer.  Its lanes fetch 32 block ids
 // of the table at a time; lane 0 issues the TMA loads (CTA-local destination) of each
@@ -23,7 +24,11 @@
 // slice ks (every KS-th unit).  Per unit a consumer computes S = Q K^T and
 // O += P V with mma.sync m16n8k16 (bf16 in, fp32 accumulate) and keeps the
 // online softmax (running max m, denominator l, rescaled O) in registers,
-// reducing row maxima across each lane quad with warp shuffles.  Key slices
+// reducing row maxima across each lane quad with warp shuffles.  Where the
+// registers allow (MmaCfg::U), a consumer takes two of its units per
+// iteration for more independent MMAs between waits; at two row tiles, and at
+// three row tiles of 4 heads (12 consumer warps), the Q fragments sit in
+// per-lane shared-memory slots (MmaCfg::QSM) instead of registers.  Key slices
 // (KS > 1) are merged through shared memory at the end of a range.  Every
 // wait is bounded and reports CX_DEV_WAIT_TIMEOUT instead of hanging.
 #include <cuda.h>
