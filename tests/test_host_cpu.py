@@ -33,6 +33,36 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert lib.cx_version().startswith(b"cxkv")
 
 
+def test_kernel_selection_rules_read_host_fields_only():
+    """cx_paged_kernel_kind decides from host fields alone, so the dispatch
+    rules hold without a GPU: bf16 pools with 16-token blocks and head_dim 64 /
+    128 take mma.sync below 64 packed rows (query tokens x GQA group) and
+    tcgen05 from 64 rows; fp32 / fp16 pools, other block sizes or head dims
+    and pools not 16-byte aligned take the generic kernel.  The pool and
+    table addresses are placeholders that nothing dereferences."""
+    lib = _lib.load_library()
+
+    def kind(*, dtype=_lib.CX_BF16, bs=16, d=128, hk=8, hq=32, q=1, verify=1,
+             q_dtype=_lib.CX_BF16, base=0x100000):
+        pool = _lib.CxPool(base, base + 0x4000000, 2, 1024, bs, hk, d, dtype, 0)
+        b = _lib.CxAttnBatch(0x200000, 64, 0x300000, 0x400000 if verify else None, 4, q,
+                             hq, float("nan"), 0, 0)
+        return _lib.KERNEL_KINDS[lib.cx_paged_kernel_kind(ctypes.byref(pool), ctypes.byref(b),
+                                                          q_dtype, verify)]
+
+    assert kind(verify=0) == "mma"                      # decode: G = 4 rows
+    assert kind(verify=0, q=50) == "mma"                # decode ignores max_q_len
+    assert kind(q=15) == "mma" and kind(q=16) == "tcgen05"   # 60 / 64 packed rows
+    assert kind(q=9) == kind(q=9, d=64) == "mma"        # 36 rows, both head dims
+    assert kind(hq=8, hk=8, q=63) == "mma" and kind(hq=8, hk=8, q=64) == "tcgen05"
+    assert kind(q=200, q_dtype=_lib.CX_F32) == "tcgen05"
+    assert kind(q=200, q_dtype=_lib.CX_F16) == "generic"
+    for bad in (dict(dtype=_lib.CX_F32), dict(dtype=_lib.CX_F16), dict(bs=32), dict(d=96),
+                dict(d=256), dict(base=0x100008)):
+        assert kind(**bad) == "generic", bad
+        assert kind(q=100, **bad) == "generic", bad
+
+
 def test_struct_layouts_match_header():
     assert ctypes.sizeof(_lib.CxPool) == 2 * 8 + 5 * 8 + 2 * 4
     assert ctypes.sizeof(_lib.CxAttnBatch) == 8 * 7 + 4 + 4 + 8
