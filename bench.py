@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["cfg2", "small", "prefill", "prefill-small",
                                          "prefill-d64", "append", "cfg4", "cfg4-small",
-                                         "copy"],
+                                         "copy", "cfg1", "cfg2-f32", "cfg5"],
                     default="cfg2",
                     help="small: 1 layer, pool sized to need (~2 GB, for profiler captures); "
                          "prefill: chunked-prefill attention on the tcgen05 kernel (its own "
@@ -58,8 +58,16 @@ def parse():
                          "cfg4-small: the same with 16 sequences (~2.4 GB, for profiler "
                          "captures); "
                          "copy: block copy (compaction) and read_layer gather (their own "
-                         "JSON lines, GB/s)")
+                         "JSON lines, GB/s); cfg1: the fp32 cfg1 32-step run (KV tokens/s, "
+                         "with the oracle port timed on it); cfg2-f32: the cfg2 decode shape "
+                         "on an fp32 pool (GB/s); cfg5: continuous-batching churn, one "
+                         "shard of 1024 lognormal sequences per GPU (run under torchrun)")
     ap.add_argument("--pool-frac", type=float, default=0.9)
+    ap.add_argument("--layers", type=int, default=32, help="cfg5: layers per step")
+    ap.add_argument("--gather", choices=["serial", "overlap"], default="serial",
+                    help="N > 1: all-gather of each step's rows on the step stream after "
+                         "its last layer (serial), or on a side stream overlapped with the "
+                         "next step (overlap)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -320,6 +328,44 @@ class AllGatherer:
             return None
         return float(np.mean([a.elapsed_time(b) for a, b in self.times]))
 
+class SerialGatherer:
+    """NCCL all-gather of each step's attention rows issued on the step's own
+    stream after its last layer: it runs when the decode grid has released
+    the SMs, instead of competing with the next step's persistent grid for
+    them (the overlapped form on a side stream did), and is timed by events
+    around it on that stream."""
+
+    def __init__(self, dist, dev, gathered):
+        self.dist, self.gathered = dist, gathered
+        self.comm = None
+        self.times = []
+
+    def issue(self, stream, rows):
+        import torch
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            self.dist.all_gather_into_tensor(self.gathered, rows)
+            e1.record(stream)
+        self.times.append((e0, e1))
+
+    def reset_timing(self):
+        self.times = []
+
+    def mean_ms(self):
+        if not self.times:
+            return None
+        return float(np.mean([a.elapsed_time(b) for a, b in self.times]))
+
+
+def make_gatherer(args, dist, dev, world, gathered, shape):
+    if world <= 1:
+        return None
+    if args.gather == "overlap":
+        return AllGatherer(dist, dev, world, gathered, shape)
+    return SerialGatherer(dist, dev, gathered)
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -380,7 +426,7 @@ def run_ours(args):
     # The per-step all-gather of the last layer's rows runs on its own stream,
     # overlapped with the next step and timed by its own events; it reads a
     # double-buffered copy so the next step never overwrites rows in flight.
-    ag = AllGatherer(dist, dev, world, gathered, (BATCH, HQ, D)) if world > 1 else None
+    ag = make_gatherer(args, dist, dev, world, gathered, (BATCH, HQ, D))
 
     def one_step(s, ev=None):
         bt = batches[s]
@@ -431,7 +477,7 @@ def run_ours(args):
             ag.reset_timing()
         for i in range(args.steps):
             one_step(args.warmup + i, evs.get(i))
-        if ag is not None:
+        if ag is not None and ag.comm is not None:
             stream.wait_stream(ag.comm)             # the timed region includes the gathers
         end.record(stream)
         torch.cuda.synchronize(dev)
@@ -535,7 +581,7 @@ def run_e2e(args, lib, pool, cache, batches, slots, layers, n_sets, dev, world, 
     sp = main.cuda_stream
     gathered = torch.empty((world * BATCH, HQ, D), dtype=torch.float32, device=dev) \
         if world > 1 else None
-    ag = AllGatherer(dist, dev, world, gathered, (BATCH, HQ, D)) if world > 1 else None
+    ag = make_gatherer(args, dist, dev, world, gathered, (BATCH, HQ, D))
     # per-step scheduler metadata also comes from the host: context lengths
     # (for the plan) and the append slots
     hctx = [b.ctx_lens.cpu().pin_memory() for b in batches]
@@ -594,7 +640,7 @@ def run_e2e(args, lib, pool, cache, batches, slots, layers, n_sets, dev, world, 
     start.record(main)
     for i in range(args.steps):
         step(args.warmup + i)
-    if ag is not None:
+    if ag is not None and ag.comm is not None:
         main.wait_stream(ag.comm)
     end.record(main)
     torch.cuda.synchronize(dev)
@@ -978,6 +1024,472 @@ def run_verify(args):
         torch.cuda.empty_cache()
 
 
+# ---------------------------------------------------------------------------
+# cfg1: the reference's CPU-runnable case, fp32 pool (separate mode)
+# ---------------------------------------------------------------------------
+def run_cfg1(args):
+    """cfg1: 8 sequences, ctx ~ U[64, 512], Hq 8 / Hkv 2, D 64, fp32 pool,
+    block tables from a permutation of 512 blocks; one timed step = the whole
+    32-step run (append one K/V token per sequence, then paged decode over the
+    full context, 32 times) from the prefilled state, so every repetition
+    rewrites the same slots with the same data.  Units = KV token-layers
+    attended over the 32 decode steps.  All of cfg1's K/V (~2.4 MB) stays in
+    L2, so this mode is launch-latency bound, not HBM bound."""
+    import torch
+    from chenxing_b200 import PagedBatch, RadixPagedKVCache, _lib
+    from chenxing_b200.batch import slot_mapping
+    from chenxing_b200.workloads import cfg1
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    wl, data = cfg1(seed=args.seed)
+    bs, B, steps = wl.block_size, wl.batch, wl.steps
+    cache = RadixPagedKVCache(wl.n_blocks, bs, 1, wl.n_kv_heads, wl.head_dim, host_io=False,
+                              device=dev)
+    for b in range(B):
+        cache.write_layer(wl.block_tables[b], 0, 0, data["k_pre"][b], data["v_pre"][b])
+    ctx0 = wl.ctx_lens.astype(np.int64)
+    stride = max(len(t) for t in wl.block_tables)
+    batches = [PagedBatch(cache, wl.block_tables, ctx0 + s + 1, n_q_heads=wl.n_q_heads,
+                          table_stride=stride) for s in range(steps)]
+    kind = batches[0].kernel_kind(torch.float32)
+    slots = [torch.from_numpy(slot_mapping(wl.block_tables, ctx0 + s, [1] * B, bs)).to(dev)
+             for s in range(steps)]
+    q = torch.from_numpy(data["q"]).to(dev)
+    k = torch.from_numpy(data["k"]).to(dev)
+    v = torch.from_numpy(data["v"]).to(dev)
+    out = torch.empty((steps, B, wl.n_q_heads, wl.head_dim), dtype=torch.float32, device=dev)
+    lib, pool = _lib.lib(), cache.cx_pool()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    units = int(sum((ctx0 + s + 1).sum() for s in range(steps)))
+    dec_ev = []
+
+    def run(timed):
+        for s in range(steps):
+            bt = batches[s]
+            _lib.check(lib.cx_kv_append(pool, 0, k[s].data_ptr(), v[s].data_ptr(), _lib.CX_F32,
+                                        slots[s].data_ptr(), B, None, None, None, 0, sp),
+                       "cx_kv_append")
+            if timed:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+                    enable_timing=True)
+                e0.record(stream)
+            _lib.check(lib.cx_paged_decode(pool, 0, bt.c_struct(), q[s].data_ptr(), _lib.CX_F32,
+                                           out[s].data_ptr(), bt.workspace.data_ptr(),
+                                           bt.workspace.numel(), 1, sp), "cx_paged_decode")
+            if timed:
+                e1.record(stream)
+                dec_ev.append((e0, e1))
+    for _ in range(args.warmup):
+        run(False)
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        run(False)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end) / args.steps
+    run(True)                                  # per-launch decode times, one extra run
+    torch.cuda.synchronize(dev)
+    if _lib.device_flags(clear=True):
+        raise RuntimeError("device flags raised during the cfg1 bench")
+    dms = float(np.mean([a.elapsed_time(b) for a, b in dec_ev]))
+    alg = units / steps * 2 * wl.n_kv_heads * wl.head_dim * 4 + \
+        B * wl.n_q_heads * wl.head_dim * 8
+    peak, pk = measured_peak()
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = cpu_cfg1_rate(args.seed)
+    print(json.dumps({
+        "metric": "cfg1 paged-decode KV tokens/s (fp32 pool, 32-step run of append + decode)",
+        "value": units / (ms / 1e3), "unit": "KV-token-layers/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "ms_per_decode_step": ms / steps, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (cfg1 seeded N(0,1) Q/K/V)",
+        "config": {"workload": "cfg1: 8 seqs, ctx U[64,512], Hq 8 / Hkv 2, D 64, fp32, "
+                               "32 decode steps per timed step", "kernel": kind,
+                   "l2": "K/V ~2.4 MB, L2-resident (launch-latency bound)"},
+        "roofline": {"bound": "latency", "kernel": "paged_attn_f32_kernel",
+                     "avg_launch_ms": dms, "algorithmic_bytes_per_launch": alg,
+                     "achieved": alg / (dms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": alg / (dms / 1e3) / 1e9 / peak, "peak_source": pk},
+        "cpu_baseline": cpu}), flush=True)
+
+
+def cpu_cfg1_rate(seed):
+    """The oracle port of the reference path on the cfg1 32-step run, one
+    host core: write_layer -> read_layer -> flash_attention per sequence per
+    step (transformer.py:87-94 minus projections)."""
+    from chenxing_b200.workloads import cfg1
+    from oracle.paged import attend_sequence
+    from oracle.radix_kv import OraclePagedKVCache
+    wl, data = cfg1(seed=seed)
+    cache = OraclePagedKVCache(wl.n_blocks, wl.block_size, 1, wl.n_kv_heads, wl.head_dim)
+    for b in range(wl.batch):
+        cache.write_layer(wl.block_tables[b], 0, 0, data["k_pre"][b], data["v_pre"][b])
+    ctx0 = wl.ctx_lens.astype(np.int64)
+    units, reps = 0, 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 10.0:
+        for s in range(wl.steps):
+            for b in range(wl.batch):
+                c = int(ctx0[b]) + s
+                attend_sequence(cache, wl.block_tables[b], c, 0, data["q"][s][b][None],
+                                data["k"][s][b][None], data["v"][s][b][None])
+                units += c + 1
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": units / dt, "unit": "KV-token-layers/s", "cores": 1, "kind": "port",
+            "sample": f"{reps} full cfg1 32-step runs (8 sequences) of write_layer -> "
+                      f"read_layer -> flash_attention (oracle restatement, NumPy fp32)"}
+
+
+# ---------------------------------------------------------------------------
+# cfg2 shape on an fp32 pool (separate mode)
+# ---------------------------------------------------------------------------
+def run_f32_decode(args):
+    """The cfg2 decode shape (64 sequences, ctx ~ U[1024, 8192], Hq 32 / Hkv 8,
+    D 128) on an fp32 pool: 8 layers per step, each an append of one token per
+    sequence and a paged decode (fp32 Q); pool sized to need, blocks scattered.
+    Per-launch decode times give the HBM roofline (K/V 4.9 GB per layer step,
+    far above L2)."""
+    import torch
+    from chenxing_b200 import PagedBatch, RadixPagedKVCache, _lib
+    from chenxing_b200.batch import slot_mapping
+    from chenxing_b200.workloads import cfg2_meta
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    layers, steps_total = 8, args.warmup + args.steps
+    n_blocks = BATCH * (-(-(8192 + steps_total) // BS)) + 64
+    wl = cfg2_meta(n_blocks=n_blocks, seed=args.seed, batch=BATCH, steps=steps_total,
+                   n_layers=layers)
+    cache = RadixPagedKVCache(n_blocks, BS, layers, HK, D, dtype=np.float32, device=dev,
+                              host_io=False)
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed)
+    for t in (cache._k, cache._v):
+        for l in range(layers):
+            t[l].normal_(0.0, 1.0 / math.sqrt(D), generator=g)
+    ctx0 = wl.ctx_lens.astype(np.int64)
+    sc = 1.0 / math.sqrt(D)
+    q = torch.randn((layers, BATCH, HQ, D), device=dev, generator=g) * sc
+    kn = torch.randn((layers, BATCH, HK, D), device=dev, generator=g) * sc
+    out = torch.empty((BATCH, HQ, D), dtype=torch.float32, device=dev)
+    stride = max(len(t) for t in wl.block_tables)
+    batches = [PagedBatch(cache, wl.block_tables, ctx0 + s + 1, n_q_heads=HQ,
+                          table_stride=stride) for s in range(steps_total)]
+    slots = [torch.from_numpy(slot_mapping(wl.block_tables, ctx0 + s, [1] * BATCH, BS)).to(dev)
+             for s in range(steps_total)]
+    kind = batches[0].kernel_kind(torch.float32)
+    lib, pool = _lib.lib(), cache.cx_pool()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    dec_ev = []
+
+    def step(s, timed):
+        bt = batches[s]
+        for l in range(layers):
+            _lib.check(lib.cx_kv_append(pool, l, kn[l].data_ptr(), kn[l].data_ptr(), _lib.CX_F32,
+                                        slots[s].data_ptr(), BATCH, None, None, None, 0, sp),
+                       "cx_kv_append")
+            if timed:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+                    enable_timing=True)
+                e0.record(stream)
+            _lib.check(lib.cx_paged_decode(pool, l, bt.c_struct(), q[l].data_ptr(), _lib.CX_F32,
+                                           out.data_ptr(), bt.workspace.data_ptr(),
+                                           bt.workspace.numel(), int(l == 0), sp),
+                       "cx_paged_decode")
+            if timed:
+                e1.record(stream)
+                dec_ev.append((e0, e1, s))
+    for s in range(args.warmup):
+        step(s, False)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(device_uuid(dev))
+    sampler.start()
+    time.sleep(0.5)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i, True)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    if _lib.device_flags(clear=True):
+        raise RuntimeError("device flags raised during the fp32 decode bench")
+    ms = start.elapsed_time(end) / args.steps
+    units = sum(int((ctx0 + args.warmup + i + 1).sum()) for i in range(args.steps)) * layers
+    dms = float(np.mean([a.elapsed_time(b) for a, b, _ in dec_ev]))
+    kv_tok = float(np.mean([int((ctx0 + s + 1).sum()) for _, _, s in dec_ev]))
+    nblk = sum(len(t) for t in wl.block_tables)
+    alg = kv_tok * 2 * HK * D * 4 + BATCH * HQ * D * 8 + 4 * nblk
+    gbs = alg / (dms / 1e3) / 1e9
+    peak, pk = measured_peak()
+    print(json.dumps({
+        "metric": "paged-decode KV tokens/s, fp32 pool (cfg2 shape)",
+        "value": units / (ms / 1e3) , "unit": "KV-token-layers/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1)/sqrt(128) K/V/Q)",
+        "config": {"workload": f"cfg2 shape on an fp32 pool: 64 seqs, ctx U[1024,8192], "
+                               f"{layers} layers per step (append + decode)", "kernel": kind,
+                   "q_heads": HQ, "kv_heads": HK, "head_dim": D, "block_size": BS,
+                   "l2": "K/V ~4.9 GB per decode launch, > 126 MB L2"},
+        "roofline": {"bound": "hbm", "kernel": "paged_attn_f32_kernel", "achieved": gbs,
+                     "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_source": pk,
+                     "algorithmic_bytes_per_launch": alg, "avg_launch_ms": dms},
+        "clocks": clocks}), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# cfg5: continuous-batching churn, one shard of 1024 sequences per GPU
+# ---------------------------------------------------------------------------
+CFG5_SEQS, CFG5_SHARDS, CFG5_PREFIX = 1024, 8, 1024
+SRC_ROWS = 1 << 16          # random K/V source rows for prompt appends
+
+
+def run_cfg5(args):
+    """cfg5: 1024 sequences with lognormal contexts (median 2048, sigma 1.0,
+    capped at 32768) split by ``partition_by_context`` into 8 shards; rank r
+    of N GPUs runs shard r (weak scaling: N = 8 is the whole of cfg5), with its
+    own block pool and radix subtree driven through ``BatchedKVEngine``
+    (Hq 32 / Hkv 8, D 128, bf16, 32 layers).  One step:
+      churn  -- 5 % of the live sequences finish (suffix published into the
+                radix tree, private blocks freed); as many are admitted (new
+                lognormal contexts, each with a 50 % chance of starting with one
+                of four popular 1024-token prefixes, which then hits the tree)
+                and their prompt K/V appended for every layer; LRU eviction of
+                16-255 blocks; compaction of the pool (one block-copy launch);
+      decode -- for each layer, append one token per live sequence and paged
+                decode over its whole context;
+      gather -- NCCL all-gather of the last layer's attention rows (N > 1).
+    Time = CUDA events on the step stream, max over ranks; value = all
+    ranks' decode KV token-layers / that time."""
+    import itertools
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+    from chenxing_b200 import RadixPagedKVCache, _lib
+    from chenxing_b200.engine import BatchedKVEngine
+    from chenxing_b200.sharding import partition_by_context
+    from chenxing_b200.workloads import lognormal_ctx
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > CFG5_SHARDS:
+        raise SystemExit(f"cfg5 has {CFG5_SHARDS} shards; run it on at most 8 GPUs")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    layers = args.layers
+    ctx_all = lognormal_ctx(CFG5_SEQS, seed=args.seed + 5)
+    shards = partition_by_context(ctx_all, CFG5_SHARDS)
+    share = shards[rank]
+    n_live = len(share)
+    max_live = max(len(sh) for sh in shards[:world])
+    rng = np.random.default_rng(1000 + rank)
+    new_ctx = iter(lognormal_ctx(8192, seed=args.seed + 50 + rank))
+    steps_total = args.warmup + args.steps
+    per_block = layers * 2 * BS * HK * D * ELEM
+    need = sum(-(-(int(ctx_all[i]) + steps_total + 1) // BS) for i in share)
+    free, _ = torch.cuda.mem_get_info(dev)
+    n_blocks = int(min(1.6 * need + 4 * CFG5_PREFIX // BS, 0.8 * free / per_block))
+    clock = itertools.count()
+    cache = RadixPagedKVCache(n_blocks, BS, layers, HK, D, dtype="bfloat16", device=dev,
+                              host_io=False, clock=lambda: float(next(clock)))
+    eng = BatchedKVEngine(cache, n_q_heads=HQ, free_private_blocks=True, publish_mode="suffix")
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    sc = 1.0 / math.sqrt(D)
+    src_k = (torch.randn((SRC_ROWS, HK, D), device=dev, generator=g) * sc).bfloat16()
+    src_v = (torch.randn((SRC_ROWS, HK, D), device=dev, generator=g) * sc).bfloat16()
+    q_in = (torch.randn((layers, max_live, HQ, D), device=dev, generator=g) * sc).bfloat16()
+    k_in = (torch.randn((layers, max_live, HK, D), device=dev, generator=g) * sc).bfloat16()
+    v_in = (torch.randn((layers, max_live, HK, D), device=dev, generator=g) * sc).bfloat16()
+    out = torch.empty((max_live, HQ, D), dtype=torch.float32, device=dev)
+    gathered = torch.empty((world * max_live, HQ, D), dtype=torch.float32, device=dev) \
+        if world > 1 else None
+    stream = torch.cuda.current_stream(dev)
+    next_id = itertools.count()
+    stats = {"admitted_tokens": 0, "evicted": 0, "moved": 0, "finished": 0, "hits": 0}
+
+    def prefill(prompts):
+        """Admit sequences and append their prompts' K/V (every layer) in
+        slot chunks of at most SRC_ROWS rows."""
+        ids = []
+        for toks in prompts:
+            sid = next(next_id)
+            s = eng.add(sid, toks)
+            stats["hits"] += s.hit_tokens > 0
+            ids.append(sid)
+        q = [len(t) - eng.seqs[i].n_tokens for i, t in zip(ids, prompts)]
+        p = eng.plan(ids, q, attend=False)
+        n = int(p.slots.numel())
+        for l in range(layers):
+            for o in range(0, n, SRC_ROWS):
+                m = min(SRC_ROWS, n - o)
+                cache.append_slots(l, src_k[:m], src_v[:m], p.slots[o:o + m])
+        eng.commit(p)
+        stats["admitted_tokens"] += n
+        return ids
+
+    def prompts_for(ctxs):
+        out_p = []
+        for c in ctxs:
+            c = max(int(c), 2)
+            if rng.random() < 0.5:
+                j = int(rng.integers(0, 4))
+                extra = max(1, c - CFG5_PREFIX)
+                out_p.append(pref[j] + [int(x) for x in rng.integers(0, 50000, size=extra)])
+            else:
+                out_p.append([int(x) for x in rng.integers(0, 50000, size=c)])
+        return out_p
+
+    # four popular prefixes, written once and published (owned by the tree)
+    pref = [[900000 + 10000 * j + i for i in range(CFG5_PREFIX)] for j in range(4)]
+    for sid in prefill(pref):
+        eng.finish(sid)
+    for o in range(0, n_live, 16):               # the shard's sequences, 16 at a time
+        prefill(prompts_for([ctx_all[i] for i in share[o:o + 16]]))
+    for k in stats:
+        stats[k] = 0
+    torch.cuda.synchronize(dev)
+
+    copy_ev, dec_ev = [], []
+    ev_steps = set(range(steps_total - 2, steps_total))
+
+    def one_step(si, timed):
+        live = sorted(eng.seqs)
+        n_fin = max(1, int(round(0.05 * len(live))))
+        for sid in rng.choice(live, size=n_fin, replace=False):
+            eng.finish(int(sid))
+        prefill(prompts_for([next(new_ctx) for _ in range(n_fin)]))
+        stats["finished"] += n_fin
+        stats["evicted"] += cache.evict(int(rng.integers(16, 256)))
+        e0 = torch.cuda.Event(enable_timing=True) if timed else None
+        if e0 is not None:
+            e0.record(stream)
+        moved = eng.compact()
+        if e0 is not None and moved:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(stream)
+            copy_ev.append((e0, e1, moved))
+        stats["moved"] += moved
+        ids = sorted(eng.seqs)
+        p = eng.plan(ids)
+        B = len(ids)
+        units = int(p.batch.ctx_host.sum()) * layers
+        for l in range(layers):
+            cache.append_slots(l, k_in[l, :B], v_in[l, :B], p.slots)
+            d0 = d1 = None
+            if si in ev_steps:
+                d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+                    enable_timing=True)
+                d0.record(stream)
+            cache.decode_batch(l, q_in[l, :B], p.batch, out[:B])
+            if d1 is not None:
+                d1.record(stream)
+                dec_ev.append((d0, d1, int(p.batch.ctx_host.sum()),
+                               sum(len(t) for t in p.batch.tables_host), B))
+        eng.commit(p)
+        if world > 1:                              # serial: the SMs are free by now
+            dist.all_gather_into_tensor(gathered, out)
+        return units
+
+    for si in range(args.warmup):
+        one_step(si, False)
+    torch.cuda.synchronize(dev)
+    for k in stats:
+        stats[k] = 0
+    if _lib.device_flags(clear=True, device=dev):
+        raise RuntimeError("device flags raised during the cfg5 warm-up")
+    sampler = ClockSampler(device_uuid(dev)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.5)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    t_host = time.perf_counter()
+    units = 0
+    for i in range(args.steps):
+        units += one_step(args.warmup + i, True)
+    t_host = time.perf_counter() - t_host
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    clocks = sampler.stop() if sampler else None
+    ms = start.elapsed_time(end)
+    flags = _lib.device_flags(clear=True, device=dev)
+    if flags:
+        raise RuntimeError(f"device flags during cfg5: {_lib.describe_flags(flags)}")
+    dms = [a.elapsed_time(b) for a, b, *_ in dec_ev]
+    dec_bytes = [c * UNIT_BYTES + bsz * HQ * D * (ELEM + 4) + 4 * nb
+                 for _, _, c, nb, bsz in dec_ev]
+    dec_gbs = float(np.mean([b / (t / 1e3) / 1e9 for b, t in zip(dec_bytes, dms)]))
+    cms = sum(a.elapsed_time(b) for a, b, _ in copy_ev)
+    cmoved = sum(m for *_, m in copy_ev)
+    copy_gbs = (cmoved * 2 * per_block) / (cms / 1e3) / 1e9 if cms > 0 else None
+    mine = {"rank": rank, "units": units, "ms": ms, "live": len(eng.seqs),
+            "kv_tokens": int(sum(s.n_tokens for s in eng.seqs.values())),
+            "host_s": t_host, "decode_gbs": dec_gbs, "n_blocks": n_blocks, **stats}
+    per_rank = [None] * world
+    if world > 1:
+        dist.all_gather_object(per_rank, mine)
+    else:
+        per_rank = [mine]
+    ms_max = max(r["ms"] for r in per_rank)
+    units_all = sum(r["units"] for r in per_rank)
+    if rank == 0:
+        peak, pk = measured_peak()
+        steps = args.steps
+        line = {
+            "metric": "cfg5 churn: paged-decode KV tokens/s (KV token-layers/s, max over ranks)",
+            "value": units_all / (ms_max / 1e3), "unit": UNIT, "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": ms_max / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded lognormal contexts, random K/V/Q)",
+            "config": {"workload": "cfg5: 1024 lognormal seqs (median 2048, sigma 1.0, cap "
+                                   "32768) in 8 context-balanced shards, rank r runs shard r; "
+                                   "per step 5 % finish, as many admitted (50 % with a "
+                                   "1024-token radix hit), LRU evict, compaction, decode",
+                       "layers": layers, "q_heads": HQ, "kv_heads": HK, "head_dim": D,
+                       "block_size": BS, "kv_dtype": "bf16", "seqs_per_rank": n_live,
+                       "parallelism": f"sequence-sharded x{world} (own pool + radix subtree)",
+                       "l2": "every decode launch reads > 126 MB of KV"},
+            "per_step": {"finished": stats["finished"] / steps,
+                         "admitted_tokens": stats["admitted_tokens"] / steps,
+                         "radix_hits": stats["hits"] / steps,
+                         "evicted_blocks": stats["evicted"] / steps,
+                         "moved_blocks": stats["moved"] / steps},
+            "compaction": {"kernel": "block_copy_vec_kernel", "gbs": copy_gbs,
+                           "blocks_moved_timed": cmoved, "ms": cms},
+            "roofline": {"bound": "hbm", "kernel": "paged_attn_mma_kernel",
+                         "achieved": dec_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": dec_gbs / peak, "peak_source": pk,
+                         "avg_launch_ms": float(np.mean(dms)),
+                         "algorithmic_bytes_per_launch": float(np.mean(dec_bytes))},
+            "per_rank": [{k: r[k] for k in ("rank", "units", "ms", "live", "kv_tokens",
+                                             "host_s", "decode_gbs")} for r in per_rank],
+            "gather": "serial all-gather of the last layer's rows after each step"
+                      if world > 1 else None,
+            "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.warmup < 3:
@@ -992,6 +1504,12 @@ def main():
         run_verify(args)
     elif args.config == "copy":
         run_copy(args)
+    elif args.config == "cfg1":
+        run_cfg1(args)
+    elif args.config == "cfg2-f32":
+        run_f32_decode(args)
+    elif args.config == "cfg5":
+        run_cfg5(args)
     else:
         run_ours(args)
 

@@ -71,6 +71,17 @@ def to_device(x, device: torch.device, *, float_only: bool = True) -> torch.Tens
     return t.to(device).contiguous()
 
 
+def upload(a, device: torch.device) -> torch.Tensor:
+    """Host metadata (NumPy) -> device without synchronising the stream: the
+    array is staged in pinned memory and copied with ``non_blocking`` on the
+    current stream (torch keeps the pinned buffer until the copy has run), so
+    the host can plan the next step while the device still runs this one."""
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if torch.device(device).type != "cuda":
+        return t
+    return t.pin_memory().to(device, non_blocking=True)
+
+
 def to_numpy(t: torch.Tensor) -> np.ndarray:
     """Device tensor -> NumPy (bf16 as ml_dtypes.bfloat16)."""
     if t.dtype == torch.bfloat16:

@@ -28,8 +28,8 @@ DEV_FLAG_NAMES = {1: "bad slot", 2: "bad block id", 4: "context longer than its 
 EXPORTS = ("cx_version", "cx_last_error", "cx_device_error", "cx_kv_append", "cx_kv_gather",
            "cx_block_copy", "cx_paged_workspace_bytes", "cx_paged_decode", "cx_paged_verify",
            "cx_attention_dense", "cx_paged_decode_static", "cx_paged_kernel_kind",
-           "cx_kv_append_rope")
-KERNEL_KINDS = {0: "generic", 1: "mma", 2: "tcgen05"}
+           "cx_kv_append_rope", "cx_set_wait_limit_ns")
+KERNEL_KINDS = {0: "generic", 1: "mma", 2: "tcgen05", 3: "fma"}
 
 
 class CxPool(ctypes.Structure):
@@ -76,6 +76,7 @@ _SIGS = {
                                 _I32, _VP, _VP], ctypes.c_int),
     "cx_paged_kernel_kind": ([ctypes.POINTER(CxPool), ctypes.POINTER(CxAttnBatch), _I32, _I32],
                              ctypes.c_int),
+    "cx_set_wait_limit_ns": ([ctypes.c_uint64], None),
     "cx_kv_append_rope": ([ctypes.POINTER(CxPool), _I64, _VP, _VP, _I32, _VP, _VP, _I64, _VP, _VP,
                            _I64, _I32, _VP, _I64, _VP, _I32, _VP], ctypes.c_int),
 }

@@ -17,7 +17,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._arrays import to_device
+from ._arrays import to_device, upload
 
 __all__ = ["PagedBatch", "slot_mapping", "decode_batch", "verify_batch"]
 
@@ -89,8 +89,8 @@ class PagedBatch:
         self.stride = stride
         self.tables_host = [list(t) for t in block_tables]
         self.ctx_host = ctx
-        self.block_tables = torch.from_numpy(tab).to(self.device)
-        self.ctx_lens = torch.from_numpy(ctx.astype(np.int32)).to(self.device)
+        self.block_tables = upload(tab, self.device)
+        self.ctx_lens = upload(ctx.astype(np.int32), self.device)
         if self.verify:
             ql = np.asarray(q_lens, dtype=np.int64).reshape(-1)
             if ql.shape[0] != B or np.any(ql < 0) or np.any(ql > ctx):
@@ -98,7 +98,7 @@ class PagedBatch:
             qs = np.zeros(B + 1, dtype=np.int64)
             np.cumsum(ql, out=qs[1:])
             self.q_lens_host = ql
-            self.q_start = torch.from_numpy(qs.astype(np.int32)).to(self.device)
+            self.q_start = upload(qs.astype(np.int32), self.device)
             self.max_q = int(ql.max(initial=1))
             self.total_q = int(qs[-1])
         else:

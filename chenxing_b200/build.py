@@ -4,11 +4,14 @@
 
 The library is one translation unit (csrc/cxkv.cu includes the parts), linked
 against the static CUDA runtime, so it only needs the NVIDIA driver at run
-time.  Rebuilds when any source or header is newer than the library.
+time.  Rebuilds unless the stamp file beside the library records the SHA-256
+of exactly the current sources, headers, nvcc flags and nvcc version (file
+times are not trusted: a library copied along with the tree keeps them).
 """
 from __future__ import annotations
 
 import glob
+import hashlib
 import os
 import shutil
 import subprocess
@@ -34,16 +37,40 @@ def nvcc() -> str:
     return cand if os.path.exists(cand) else (shutil.which("nvcc") or "nvcc")
 
 
+STAMP = LIB + ".sha256"
+
+
+def nvcc_version() -> str:
+    try:
+        return subprocess.run([nvcc(), "--version"], capture_output=True, text=True).stdout
+    except OSError:
+        return "nvcc missing"
+
+
+def content_hash() -> str:
+    """SHA-256 over every source and header (path and bytes), the nvcc
+    command-line flags and the nvcc version."""
+    h = hashlib.sha256()
+    for path in sources():
+        h.update(os.path.relpath(path, ROOT).encode())
+        with open(path, "rb") as f:
+            h.update(f.read())
+    h.update(repr((ARCH, FLAGS)).encode())
+    h.update(nvcc_version().encode())
+    return h.hexdigest()
+
+
 def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+    if not os.path.exists(LIB) or not os.path.exists(STAMP):
         return False
-    t = os.path.getmtime(LIB)
-    return all(os.path.getmtime(s) <= t for s in sources())
+    with open(STAMP) as f:
+        return f.read().strip() == content_hash()
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return LIB
+    digest = content_hash()
     tmp = LIB + ".tmp"
     cmd = [nvcc(), *ARCH, *FLAGS, "-I", os.path.join(ROOT, "include"),
            os.path.join(HERE, "csrc", "cxkv.cu"), "-o", tmp]
@@ -54,6 +81,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if verbose:
         sys.stderr.write(res.stderr)
     os.replace(tmp, LIB)
+    with open(STAMP, "w") as f:
+        f.write(digest + "\n")
     return LIB
 
 

@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "cx_common.cuh"  // unity build: included from cxkv.cu
@@ -42,6 +43,11 @@ namespace cx {
 
 constexpr int kBlockTok = 16;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+// Limit of the decode / verify pipeline waits (default kWaitLimitNs).  A test
+// shortens it (cx_set_wait_limit_ns) to make the waits run out on purpose and
+// check that the kernel returns with CX_DEV_WAIT_TIMEOUT raised.
+static std::atomic<unsigned long long> g_wait_limit_ns{kWaitLimitNs};
 constexpr int kPlanMagic = 0x43584b56;                       // "CXKV"
 constexpr int kMinUnitsPerCta = 4;
 constexpr int kConsumerWarps = 8;
@@ -57,6 +63,9 @@ struct MmaParams {
     int32_t n_blocks, layer, window;
     int32_t stages, stage_bytes;
     float scale_log2;
+    uint64_t wait_ns;    // limit of every pipeline wait (cx_set_wait_limit_ns)
+    int32_t ks, mt;      // fp32 kernel: key slices and row tiles (runtime)
+    int32_t q_bf16;      // fp32 kernel: q is bf16 (else fp32)
     const void* q;
     float* out;
     int32_t* plan;       // [16] header: W, chunk, P_eff, magic, batch, n_groups
@@ -179,6 +188,215 @@ struct SegCursor {
     }
 };
 
+// ---------------------------------------------------------------------------
+// TMA producer (the last warp of a decode / verify CTA), shared by the bf16
+// mma.sync kernel and the fp32 FMA kernel: for every unit of the CTA's chunk,
+// in order, wait for its ring stage to be free, then load the unit's K and V
+// (HG heads x 16 tokens x head_dim) as NBOX column boxes of 128 bytes each
+// (BOX_COLS elements, 128-byte swizzle) with 3-D TMA tile loads into this
+// CTA's own shared memory; a block id outside the pool loads nothing and
+// marks the stage bad.  Lanes fetch 32 block ids of the table per load; lane
+// 0 issues.  Every wait is bounded; after a give-up (own or a consumer's) no
+// stage is re-armed, and before returning the producer waits for its own
+// copies still in flight.
+// ---------------------------------------------------------------------------
+template <int NBOX, int BOX_COLS, int BOX_BYTES, int TILES, int STAGE>
+__device__ __forceinline__ void produce_units(const CUtensorMap* tmk, const CUtensorMap* tmv,
+                                              const MmaParams& p, SegCursor cur, int HG,
+                                              unsigned char* ring, uint64_t* full_bar,
+                                              uint64_t* empty_bar, volatile int* s_abort,
+                                              volatile unsigned char* s_bad, int lane) {
+    const int STAGES = p.stages;
+    Seg seg;
+    int i = 0, issued = 0;
+    bool aborted = false;
+    while (cur.next(seg)) {
+        const int32_t* bt = p.tables + (int64_t)seg.b * p.table_stride;
+        const int zh = seg.g * HG;
+        for (int k0 = 0; k0 < seg.cnt; k0 += 32) {
+            const int n = min(32, seg.cnt - k0);
+            int bid = -1;
+            if (lane < n) {
+                const int jj = seg.j0 + k0 + lane;
+                bid = jj < p.table_stride ? bt[jj] : -1;
+                if (bid < 0 || bid >= p.n_blocks) {
+                    raise_flag(CX_DEV_BAD_BLOCK);
+                    bid = -1;
+                }
+            }
+            for (int k = 0; k < n; ++k, ++i) {
+                const int bk = __shfl_sync(0xffffffffu, bid, k);
+                if (lane == 0 && !aborted) {
+                    const int s = i % STAGES;
+                    const uint32_t par = ((i / STAGES) & 1) ^ 1;
+                    if (!mbar_wait_bounded(&empty_bar[s], par, s_abort, p.wait_ns)) {
+                        aborted = true;
+                        *s_abort = 1;
+                        raise_flag(CX_DEV_WAIT_TIMEOUT);
+                    } else if (*s_abort) {
+                        // A consumer gave up and released this stage without
+                        // waiting for its previous fill, whose bytes may still
+                        // be landing: never re-arm it.
+                        aborted = true;
+                    } else if (bk >= 0) {
+                        s_bad[s] = 0;
+                        mbar_arrive_expect_tx(&full_bar[s], STAGE);
+                        const int z = (p.layer * p.n_blocks + bk) * p.hk + zh;
+                        unsigned char* kd = ring + (size_t)s * STAGE;
+#pragma unroll
+                        for (int c = 0; c < NBOX; ++c) {
+                            tma_load_3d(kd + c * BOX_BYTES, tmk, &full_bar[s], c * BOX_COLS, 0, z);
+                            tma_load_3d(kd + TILES + c * BOX_BYTES, tmv, &full_bar[s],
+                                        c * BOX_COLS, 0, z);
+                        }
+                    } else {
+                        // bad id: nothing is loaded; the consumers see the flag
+                        // and leave the stage's keys out
+                        s_bad[s] = 1;
+                        mbar_arrive(&full_bar[s]);
+                    }
+                    if (!aborted) ++issued;
+                }
+                __syncwarp();
+            }
+        }
+    }
+    // Do not leave the CTA with tile copies still landing in its smem (a fixed
+    // limit: the copies land within microseconds unless the GPU is broken, and
+    // a short test limit must not cut this wait).
+    if (lane == 0) {
+        const int first = issued > STAGES ? issued - STAGES : 0;
+        for (int t = first; t < issued; ++t) {
+            if (!mbar_wait_bounded(&full_bar[t % STAGES], (t / STAGES) & 1, nullptr,
+                                   kWaitLimitNs)) {
+                raise_flag(CX_DEV_WAIT_TIMEOUT);
+                break;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// End of a (sequence, head group) range, shared by the decode / verify
+// kernels.  Partial softmax states are rows of D + 2 floats: the unnormalised
+// O, the running max m (base-2 domain) and the denominator l.
+// ---------------------------------------------------------------------------
+// Merge the KS key slices of the CTA from shared memory (`merge`,
+// [KS][HG][p.rows][D + 2], filled by every consumer warp) into the final rows
+// (a range wholly inside this CTA) or into the CTA's workspace slot.
+template <int D, int HG>
+__device__ __forceinline__ void ks_merge(const MmaParams& p, const float* merge, float* slot,
+                                         const Seg& seg, int64_t qs, int rows_b, int ctid,
+                                         int NCT, int KS) {
+    const int G = p.group, Hq = p.hq;
+    named_bar_sync(1, NCT);
+    for (int e = ctid; e < HG * rows_b * D; e += NCT) {
+        const int d = e % D;
+        const int R = (e / D) % rows_b;
+        const int eh = e / (D * rows_b);
+        float M = -INFINITY;
+#pragma unroll 4
+        for (int s2 = 0; s2 < KS; ++s2)
+            M = fmaxf(M, merge[(((size_t)s2 * HG + eh) * p.rows + R) * (D + 2) + D]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll 4
+            for (int s2 = 0; s2 < KS; ++s2) {
+                const float* r = merge + (((size_t)s2 * HG + eh) * p.rows + R) * (D + 2);
+                const float wgt = exp2f(r[D] - M);
+                L += r[D + 1] * wgt;
+                O += r[d] * wgt;
+            }
+        }
+        if (seg.whole) {
+            const int64_t orow = (qs + R / G) * Hq + (int64_t)(seg.g * HG + eh) * G + R % G;
+            p.out[orow * D + d] = L > 0.f ? O / L : 0.f;
+        } else {
+            float* r = slot + ((size_t)eh * p.rows + R) * (D + 2);
+            r[d] = O;
+            if (d == 0) {
+                r[D] = M;
+                r[D + 1] = L;
+            }
+        }
+    }
+}
+
+// A range cut by a chunk boundary: every CTA holding part of it takes an
+// atomic ticket after writing its slot; the last one merges all partials of
+// the range in one pass (log-sum-exp) and writes the final rows.  No waiting.
+template <int D, int HG>
+__device__ __forceinline__ void ticket_merge(const MmaParams& p, const Seg& seg, int b,
+                                             int64_t qs, int rows_b, int ctid, int NCT,
+                                             int chunk, int* s_last) {
+    const int G = p.group, Hq = p.hq;
+    const int bg = b * p.n_groups + seg.g;
+    const size_t slot_floats = (size_t)HG * p.rows * (D + 2);
+    __threadfence();
+    named_bar_sync(1, NCT);
+    if (ctid == 0) {
+        const int first_u = p.seq_start[b] + seg.g * seg.nb;
+        const int pf = first_u / chunk, pl = (first_u + seg.nb - 1) / chunk;
+        const int prev = atomicAdd(&p.counters[bg], 1);
+        *s_last = (prev == pl - pf) ? (pf | (pl << 16)) + 1 : 0;
+    }
+    named_bar_sync(1, NCT);
+    const int last = *s_last;
+    if (!last) return;
+    __threadfence();
+    const int pf = (last - 1) & 0xffff, pl = (last - 1) >> 16;
+    // one pass over the partials, two columns per thread: the loads of every
+    // partial are independent of the running merge, so they overlap instead
+    // of costing an L2 round trip each
+    constexpr int D2 = D / 2;
+    for (int e = ctid; e < HG * rows_b * D2; e += NCT) {
+        const int d = 2 * (e % D2);
+        const int R = (e / D2) % rows_b;
+        const int eh = e / (D2 * rows_b);
+        const float* r0 = p.partials + (size_t)(pf + bg) * slot_floats +
+                          ((size_t)eh * p.rows + R) * (D + 2);
+        float M = -INFINITY, L = 0.f, Ox = 0.f, Oy = 0.f;
+#pragma unroll 4
+        for (int pp = 0; pp <= pl - pf; ++pp) {
+            const float* r = r0 + (size_t)pp * slot_floats;
+            const float m = __ldcg(r + D), l = __ldcg(r + D + 1);
+            const float2 o = __ldcg(reinterpret_cast<const float2*>(r + d));
+            if (m == -INFINITY) continue;  // a partial that saw no key
+            const float Mn = fmaxf(M, m);
+            const float a = exp2f(M - Mn), w = exp2f(m - Mn);
+            L = L * a + l * w;
+            Ox = Ox * a + o.x * w;
+            Oy = Oy * a + o.y * w;
+            M = Mn;
+        }
+        const int64_t orow = (qs + R / G) * Hq + (int64_t)(seg.g * HG + eh) * G + R % G;
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        *reinterpret_cast<float2*>(p.out + orow * D + d) =
+            L > 0.f ? make_float2(Ox * inv, Oy * inv) : make_float2(0.f, 0.f);
+    }
+    if (ctid == 0) p.counters[bg] = 0;
+}
+
+// The plan must come from paged_plan_kernel for this batch shape (else the
+// flag is raised and the CTA returns false); sequences with no cached token
+// get zero rows (naive_attention semantics for rows with no key).
+template <int D>
+__device__ __forceinline__ bool plan_ok_zero_empty(const MmaParams& p) {
+    const int B = p.batch, Hq = p.hq, tid = threadIdx.x;
+    if (p.plan[3] != kPlanMagic || p.plan[4] != B || p.plan[5] != p.n_groups) {
+        if (tid == 0 && blockIdx.x == 0) raise_flag(CX_DEV_BAD_QLEN);
+        return false;
+    }
+    for (int b = blockIdx.x; b < B; b += gridDim.x) {
+        if (p.seq_start[b + 1] != p.seq_start[b]) continue;
+        const int sq = p.q_start ? p.q_start[b + 1] - p.q_start[b] : 1;
+        const int64_t r0 = p.q_start ? p.q_start[b] : b;
+        for (int64_t e = tid; e < (int64_t)sq * Hq * D; e += blockDim.x)
+            p.out[r0 * Hq * D + e] = 0.f;
+    }
+    return true;
+}
+
 template <typename QT> struct QLoad;
 template <> struct QLoad<float> {
     __device__ __forceinline__ static float2 two(const float* q, int64_t i) {
@@ -266,6 +484,8 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
                                           C::merge_bytes(p.rows));
     volatile int* s_abort = s_flags;
     int* s_last = s_flags + 1;
+    // per ring stage: 1 when its block id was outside the pool (nothing loaded)
+    volatile unsigned char* s_bad = reinterpret_cast<unsigned char*>(s_flags + 4);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int B = p.batch, Hq = p.hq, G = p.group;
@@ -277,19 +497,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
         return;
     }
 
-    // The plan must come from paged_plan_kernel for this batch shape.
-    if (p.plan[3] != kPlanMagic || p.plan[4] != B || p.plan[5] != p.n_groups) {
-        if (tid == 0 && blockIdx.x == 0) raise_flag(CX_DEV_BAD_QLEN);
-        return;
-    }
-    // Sequences with no cached token produce zero rows.
-    for (int b = blockIdx.x; b < B; b += gridDim.x) {
-        if (p.seq_start[b + 1] != p.seq_start[b]) continue;
-        const int sq = p.q_start ? p.q_start[b + 1] - p.q_start[b] : 1;
-        const int64_t r0 = p.q_start ? p.q_start[b] : b;
-        for (int64_t e = tid; e < (int64_t)sq * Hq * D; e += blockDim.x)
-            p.out[r0 * Hq * D + e] = 0.f;
-    }
+    if (!plan_ok_zero_empty<D>(p)) return;
     const int W = p.plan[0], chunk = p.plan[1], P_eff = p.plan[2];
     if ((int)blockIdx.x >= P_eff) return;
     const int u0 = blockIdx.x * chunk;
@@ -311,63 +519,8 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
     Seg seg;
 
     if (warp == C::NCW) {
-        // ------------------------------ producer ------------------------------
-        int i = 0, issued = 0;
-        bool aborted = false;
-        while (cur.next(seg)) {
-            const int32_t* bt = p.tables + (int64_t)seg.b * p.table_stride;
-            const int zh = seg.g * HG;
-            for (int k0 = 0; k0 < seg.cnt; k0 += 32) {
-                const int n = min(32, seg.cnt - k0);
-                int bid = -1;
-                if (lane < n) {
-                    const int jj = seg.j0 + k0 + lane;
-                    bid = jj < p.table_stride ? bt[jj] : -1;
-                    if (bid < 0 || bid >= p.n_blocks) {
-                        raise_flag(CX_DEV_BAD_BLOCK);
-                        bid = -1;
-                    }
-                }
-                for (int k = 0; k < n; ++k, ++i) {
-                    const int bk = __shfl_sync(0xffffffffu, bid, k);
-                    if (lane == 0 && !aborted) {
-                        const int s = i % STAGES;
-                        const uint32_t par = ((i / STAGES) & 1) ^ 1;
-                        if (!mbar_wait_bounded(&empty_bar[s], par, s_abort, kWaitLimitNs)) {
-                            aborted = true;
-                            *s_abort = 1;
-                            raise_flag(CX_DEV_WAIT_TIMEOUT);
-                        } else if (bk >= 0) {
-                            mbar_arrive_expect_tx(&full_bar[s], C::STAGE);
-                            const int z = (p.layer * p.n_blocks + bk) * p.hk + zh;
-                            unsigned char* kd = ring + (size_t)s * C::STAGE;
-#pragma unroll
-                            for (int half = 0; half < D / 64; ++half) {
-                                tma_load_3d(kd + half * (HG * C::HALF_BOX), &tmk, &full_bar[s],
-                                            half * 64, 0, z);
-                                tma_load_3d(kd + C::TILES + half * (HG * C::HALF_BOX), &tmv,
-                                            &full_bar[s], half * 64, 0, z);
-                            }
-                        } else {
-                            mbar_arrive(&full_bar[s]);  // bad id: release the slot, data unused
-                        }
-                        if (!aborted) ++issued;
-                    }
-                    __syncwarp();
-                }
-            }
-        }
-        // Do not leave the CTA with tile copies still landing in its smem.
-        if (lane == 0) {
-            const int first = issued > STAGES ? issued - STAGES : 0;
-            for (int t = first; t < issued; ++t) {
-                if (!mbar_wait_bounded(&full_bar[t % STAGES], (t / STAGES) & 1, nullptr,
-                                       kWaitLimitNs)) {
-                    raise_flag(CX_DEV_WAIT_TIMEOUT);
-                    break;
-                }
-            }
-        }
+        produce_units<D / 64, 64, HG * C::HALF_BOX, C::TILES, C::STAGE>(
+            &tmk, &tmv, p, cur, HG, ring, full_bar, empty_bar, s_abort, s_bad, lane);
         return;
     }
 
@@ -390,7 +543,9 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
     while (cur.next(seg)) {
         const int b = seg.b, h = seg.g * HG + hh;
         const int ctx = min(p.ctx_lens[b], (int)(p.table_stride * kBlockTok));
-        const int sq = p.q_start ? p.q_start[b + 1] - p.q_start[b] : 1;
+        // clamped: a query run longer than max_q_len (flagged by the plan) must
+        // not index rows past the partial / merge rows the call was sized for
+        const int sq = p.q_start ? min(max(p.q_start[b + 1] - p.q_start[b], 0), p.max_q) : 1;
         const int64_t qs = p.q_start ? p.q_start[b] : b;
         const int rows_b = G * sq;
         const int pos0 = ctx - sq;  // position of query row 0
@@ -445,7 +600,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
                 const int i = ibase + k + u * KS;
                 if (ok && (u == 0 || two))
                     ok = mbar_wait_bounded(&full_bar[su[u]], (i / STAGES) & 1, s_abort,
-                                           kWaitLimitNs);
+                                           p.wait_ns);
             }
             // mma.sync / ldmatrix need the whole warp: agree on one outcome
             ok = __all_sync(0xffffffffu, ok);
@@ -455,10 +610,16 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
                     raise_flag(CX_DEV_WAIT_TIMEOUT);
                 }
             } else {
+                // a stage whose block id was bad holds no data: its keys are
+                // left out (scores -inf, no PV product), as the generic kernel
+                // skips them (the flag is per stage, so warp-uniform)
+                bool bad[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) bad[u] = (u == 0 || two) && s_bad[su[u]] != 0;
                 float x[U][2][4];
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    if (u > 0 && !two) {
+                    if ((u > 0 && !two) || bad[u]) {
 #pragma unroll
                         for (int n = 0; n < 2; ++n)
 #pragma unroll
@@ -563,7 +724,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
                 }
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    if (u > 0 && !two) continue;
+                    if ((u > 0 && !two) || bad[u]) continue;
                     const uint32_t vb = smem_addr(ring + (size_t)su[u] * C::STAGE) + C::TILES;
                     uint32_t pa[4];
                     pa[0] = pack_bf16(pr[u][0][0], pr[u][0][1]);
@@ -642,91 +803,17 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
                     }
                 }
             }
-            named_bar_sync(1, NCT);
-            for (int e = ctid; e < HG * rows_b * D; e += NCT) {
-                const int d = e % D;
-                const int R = (e / D) % rows_b;
-                const int eh = e / (D * rows_b);
-                float M = -INFINITY;
-#pragma unroll
-                for (int s2 = 0; s2 < KS; ++s2)
-                    M = fmaxf(M, merge[(((size_t)s2 * HG + eh) * p.rows + R) * (D + 2) + D]);
-                float L = 0.f, O = 0.f;
-                if (M != -INFINITY) {
-#pragma unroll
-                    for (int s2 = 0; s2 < KS; ++s2) {
-                        const float* r = merge + (((size_t)s2 * HG + eh) * p.rows + R) * (D + 2);
-                        const float wgt = exp2f(r[D] - M);
-                        L += r[D + 1] * wgt;
-                        O += r[d] * wgt;
-                    }
-                }
-                if (seg.whole) {
-                    const int64_t orow =
-                        (qs + R / G) * Hq + (int64_t)(seg.g * HG + eh) * G + R % G;
-                    p.out[orow * D + d] = L > 0.f ? O / L : 0.f;
-                } else {
-                    float* r = slot + ((size_t)eh * p.rows + R) * (D + 2);
-                    r[d] = O;
-                    if (d == 0) {
-                        r[D] = M;
-                        r[D + 1] = L;
-                    }
-                }
-            }
+            ks_merge<D, HG>(p, merge, slot, seg, qs, rows_b, ctid, NCT, KS);
         }
-        if (!seg.whole) {
-            __threadfence();
-            named_bar_sync(1, NCT);
-            if (ctid == 0) {
-                const int first_u = p.seq_start[b] + seg.g * seg.nb;
-                const int pf = first_u / chunk, pl = (first_u + seg.nb - 1) / chunk;
-                const int prev = atomicAdd(&p.counters[bg], 1);
-                *s_last = (prev == pl - pf) ? (pf | (pl << 16)) + 1 : 0;
-            }
-            named_bar_sync(1, NCT);
-            const int last = *s_last;
-            if (last) {
-                __threadfence();
-                const int pf = (last - 1) & 0xffff, pl = (last - 1) >> 16;
-                // one pass over the partials, two columns per thread: the loads
-                // of every partial are independent of the running merge, so
-                // they overlap instead of costing an L2 round trip each
-                constexpr int D2 = D / 2;
-                for (int e = ctid; e < HG * rows_b * D2; e += NCT) {
-                    const int d = 2 * (e % D2);
-                    const int R = (e / D2) % rows_b;
-                    const int eh = e / (D2 * rows_b);
-                    const float* r0 = p.partials + (size_t)(pf + bg) * slot_floats +
-                                      ((size_t)eh * p.rows + R) * (D + 2);
-                    float M = -INFINITY, L = 0.f, Ox = 0.f, Oy = 0.f;
-#pragma unroll 4
-                    for (int pp = 0; pp <= pl - pf; ++pp) {
-                        const float* r = r0 + (size_t)pp * slot_floats;
-                        const float m = __ldcg(r + D), l = __ldcg(r + D + 1);
-                        const float2 o = __ldcg(reinterpret_cast<const float2*>(r + d));
-                        if (m == -INFINITY) continue;  // a partial that saw no key
-                        const float Mn = fmaxf(M, m);
-                        const float a = exp2f(M - Mn), w = exp2f(m - Mn);
-                        L = L * a + l * w;
-                        Ox = Ox * a + o.x * w;
-                        Oy = Oy * a + o.y * w;
-                        M = Mn;
-                    }
-                    const int64_t orow = (qs + R / G) * Hq + (int64_t)(seg.g * HG + eh) * G + R % G;
-                    const float inv = L > 0.f ? 1.f / L : 0.f;
-                    *reinterpret_cast<float2*>(p.out + orow * D + d) =
-                        L > 0.f ? make_float2(Ox * inv, Oy * inv) : make_float2(0.f, 0.f);
-                }
-                if (ctid == 0) p.counters[bg] = 0;
-            }
-        }
+        if (!seg.whole)
+            ticket_merge<D, HG>(p, seg, b, qs, rows_b, ctid, NCT, chunk, s_last);
         named_bar_sync(1, NCT);
     }
 }
 
 }  // namespace cx
 
+#include "attn_paged_f32.cuh"
 #include "attn_prefill_tc.cuh"
 #include "attn_prefill_tc128.cuh"
 #include "attn_prefill_tc256.cuh"
@@ -750,18 +837,22 @@ static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
     return fn;
 }
 
-// 3-D view of a bf16 pool: (head_dim, 16 slots, layers*blocks*heads tiles),
-// box 64 x 16 x hg (hg consecutive heads of one block) with 128-byte swizzle.
+// 3-D view of a bf16 or fp32 pool: (head_dim, 16 slots, layers*blocks*heads
+// tiles), box of one 128-byte column (64 bf16 or 32 fp32 values) x 16 x hg
+// (hg consecutive heads of one block) with 128-byte swizzle.
 static int make_pool_tmap(CUtensorMap* m, void* base, const cx_pool* p, int hg) {
     auto enc = tmap_encoder();
     if (!enc) return fail(CX_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const bool f32 = p->dtype == CX_F32;
+    const cuuint64_t e = f32 ? 4 : 2;
     const cuuint64_t dims[3] = {(cuuint64_t)p->head_dim, (cuuint64_t)p->block_size,
                                 (cuuint64_t)(p->n_layers * p->n_blocks * p->n_kv_heads)};
-    const cuuint64_t strides[2] = {(cuuint64_t)p->head_dim * 2,
-                                   (cuuint64_t)(p->block_size * p->head_dim * 2)};
-    const cuuint32_t box[3] = {64, (cuuint32_t)p->block_size, (cuuint32_t)hg};
+    const cuuint64_t strides[2] = {(cuuint64_t)p->head_dim * e,
+                                   (cuuint64_t)(p->block_size * p->head_dim * e)};
+    const cuuint32_t box[3] = {(cuuint32_t)(128 / e), (cuuint32_t)p->block_size, (cuuint32_t)hg};
     const cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+    CUresult r = enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                     3, base, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(CX_ERR_CUDA, "cuTensorMapEncodeTiled failed");
@@ -790,12 +881,39 @@ static MmaShape mma_shape(int64_t hk, int64_t rows) {
     return s;
 }
 
+// fp32 pools: heads per unit and row tiles of RT = 4, 8 or 16 rows.  One
+// head's K (or V) of a unit is 4 KB (head_dim 64) or 8 KB (128) of fp32, and
+// each TMA box covers a 128-byte column of hg heads (hg x 2 KB): a single
+// issuing thread keeps up with HBM only from about 4 KB a box, so hg is 2 or 4
+// where the KV head count allows (stage = hg x 16 KB or hg x 32 KB).  The key
+// slices (ks) are chosen at launch from the ring length.
+static int f32_rt(int64_t rows) { return rows <= 4 ? 4 : rows <= 8 ? 8 : 16; }
+
+static MmaShape f32_shape(int64_t hk, int64_t rows, int64_t d) {
+    MmaShape s{};
+    const int rt = f32_rt(rows);
+    s.mt = (int)((rows + rt - 1) / rt);
+    const int cap = d == 64 ? 4 : 2;
+    // consumer warps available: 7 for the wide row tiles (F32Cfg::MAX_CONSUMERS)
+    const int warps = (rt == 16 || (rt == 8 && d == 128)) ? 7 : kConsumerWarps;
+    s.hg = 1;
+    while (s.hg * 2 <= cap && hk % (s.hg * 2) == 0 && s.hg * 2 * s.mt <= warps) s.hg *= 2;
+    s.ks = 0;
+    s.n_groups = (int)(hk / s.hg);
+    return s;
+}
+
+static MmaShape unit_shape(const cx_pool* pool, int64_t rows) {
+    return pool->dtype == CX_F32 ? f32_shape(pool->n_kv_heads, rows, pool->head_dim)
+                                 : mma_shape(pool->n_kv_heads, rows);
+}
+
 struct WsLayout {
     size_t plan, seq, lo, cnt, part, total;
 };
 
-static WsLayout ws_layout(int64_t batch, int64_t hk, int64_t rows, int64_t d, int64_t grid) {
-    const MmaShape sh = mma_shape(hk, rows);
+static WsLayout ws_layout(int64_t batch, const MmaShape& sh, int64_t rows, int64_t d,
+                          int64_t grid) {
     auto up = [](size_t x, size_t a) { return (x + a - 1) / a * a; };
     WsLayout w{};
     w.plan = 0;
@@ -835,6 +953,62 @@ static int launch_mma_d(const MmaShape& sh, const CUtensorMap& tk, const CUtenso
     return fail(CX_ERR_UNSUPPORTED, "paged attention: no kernel for this row/head shape");
 }
 
+template <int D, int HG, int RT>
+static int launch_f32_cfg(const CUtensorMap& tk, const CUtensorMap& tv, MmaParams p,
+                          cudaStream_t st, int grid) {
+    using C = F32Cfg<D, HG, RT>;
+    auto kern = paged_attn_f32_kernel<D, HG, RT>;
+    // key slices: the ring length must be a multiple of them (each stage is
+    // always consumed by the same slice); take the longest ring, and on a tie
+    // the most consumer warps
+    const int max_ks = C::MAX_CONSUMERS / (HG * p.mt);
+    int best_ks = 0, best_st = 0;
+    for (int ks = 1; ks <= max_ks; ++ks) {
+        const int stg = (C::raw_stages(p.rows, p.mt, ks) / ks) * ks;
+        if (stg >= 2 && stg >= best_st) {
+            best_st = stg;
+            best_ks = ks;
+        }
+    }
+    if (!best_ks) return fail(CX_ERR_UNSUPPORTED, "paged attention: shared memory too small");
+    p.ks = best_ks;
+    p.stages = best_st;
+    p.stage_bytes = C::STAGE;
+    const size_t smem = C::smem_bytes(p.rows, p.mt, p.ks, p.stages);
+    const int threads = (HG * p.mt * p.ks + 1) * 32;
+    CX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<grid, threads, smem, st>>>(tk, tv, p);
+    return check_launch("paged_attn_f32_kernel");
+}
+
+template <int D>
+static int launch_f32_d(const MmaShape& sh, const CUtensorMap& tk, const CUtensorMap& tv,
+                        const MmaParams& p, cudaStream_t st, int grid) {
+    const int rt = f32_rt(p.rows);
+#define CX_CASE(HG_, RT_) \
+    if (sh.hg == HG_ && rt == RT_) return launch_f32_cfg<D, HG_, RT_>(tk, tv, p, st, grid);
+    CX_CASE(1, 4) CX_CASE(1, 8) CX_CASE(1, 16)
+    CX_CASE(2, 4) CX_CASE(2, 8) CX_CASE(2, 16)
+    if constexpr (D == 64) {
+        CX_CASE(4, 4) CX_CASE(4, 8) CX_CASE(4, 16)
+    }
+#undef CX_CASE
+    return fail(CX_ERR_UNSUPPORTED, "paged attention: no fp32 kernel for this row/head shape");
+}
+
+// fp32 pool, 16-token blocks, head_dim 64 / 128, at most 64 packed query rows
+// per KV head: the TMA + FMA kernel (attn_paged_f32.cuh)
+static bool f32_eligible(const cx_pool* pool, const cx_attn_batch* b, int32_t q_dtype) {
+    const int64_t G = b->n_q_heads / pool->n_kv_heads;
+    const int64_t rows = G * b->max_q_len;
+    const int64_t tiles = pool->n_layers * pool->n_blocks * pool->n_kv_heads;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(pool->k) | reinterpret_cast<uintptr_t>(pool->v);
+    return pool->dtype == CX_F32 && pool->block_size == kBlockTok &&
+           (pool->head_dim == 64 || pool->head_dim == 128) && rows >= 1 && rows <= 64 &&
+           (q_dtype == CX_F32 || q_dtype == CX_BF16) && tiles < (1ll << 31) && (a & 15) == 0 &&
+           b->batch < (1 << 24) && pool->n_kv_heads * b->batch < (1 << 24);
+}
+
 static bool mma_eligible(const cx_pool* pool, const cx_attn_batch* b, int32_t q_dtype) {
     const int64_t G = b->n_q_heads / pool->n_kv_heads;
     const int64_t rows = G * b->max_q_len;
@@ -847,6 +1021,23 @@ static bool mma_eligible(const cx_pool* pool, const cx_attn_batch* b, int32_t q_
 }
 
 static int grid_size() { return num_sms(); }
+
+// Scratch bytes a decode (verify = false) or verify call will use: the plan /
+// split-K workspace of the mma.sync and fp32 FMA kernels; none for the
+// tcgen05 and generic kernels.  Same kernel choice as paged_attention.
+static size_t paged_scratch_need(const cx_pool* pool, const cx_attn_batch* bt, const void* q,
+                                 int32_t q_dtype, const float* out, bool verify) {
+    if (!pool || !bt || pool->n_kv_heads <= 0 || bt->n_q_heads <= 0 || bt->batch <= 0) return 0;
+    cx_attn_batch b = *bt;
+    b.max_q_len = verify ? (bt->max_q_len > 0 ? bt->max_q_len : 1) : 1;
+    const bool vec_ok =
+        ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+    if (vec_ok && tc_eligible(pool, &b, q_dtype)) return 0;
+    const bool use_f32 = vec_ok && f32_eligible(pool, &b, q_dtype);
+    if (!use_f32 && (!vec_ok || !mma_eligible(pool, &b, q_dtype))) return 0;
+    const int64_t rows = (b.n_q_heads / pool->n_kv_heads) * b.max_q_len;
+    return ws_layout(b.batch, unit_shape(pool, rows), rows, pool->head_dim, grid_size()).total;
+}
 
 static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_batch* bt,
                            const void* q, int32_t q_dtype, float* out, void* ws,
@@ -917,7 +1108,8 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
                                  : launch_tc256<64, __nv_bfloat16>(tk, tv, t, st);
     }
 
-    if (!vec_ok || !mma_eligible(pool, &b, q_dtype)) {
+    const bool use_f32 = vec_ok && f32_eligible(pool, &b, q_dtype);
+    if (!use_f32 && (!vec_ok || !mma_eligible(pool, &b, q_dtype))) {
         GenericParams g{};
         g.q = q;
         g.out = out;
@@ -944,9 +1136,9 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
 
     const int64_t G = b.n_q_heads / pool->n_kv_heads;
     const int64_t rows = G * max_q;
-    const MmaShape sh = mma_shape(pool->n_kv_heads, rows);
+    const MmaShape sh = unit_shape(pool, rows);
     const int grid = grid_size();
-    const WsLayout wl = ws_layout(b.batch, pool->n_kv_heads, rows, pool->head_dim, grid);
+    const WsLayout wl = ws_layout(b.batch, sh, rows, pool->head_dim, grid);
     if (!ws || ws_bytes < wl.total)
         return fail(CX_ERR_WORKSPACE, "paged attention: workspace missing or too small");
     if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0)
@@ -968,10 +1160,13 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
     p.rows = (int)rows;
     p.hg = sh.hg;
     p.n_groups = sh.n_groups;
+    p.mt = sh.mt;
+    p.q_bf16 = q_dtype == CX_BF16;
     p.n_blocks = (int)pool->n_blocks;
     p.layer = (int)layer;
     p.window = b.window > 0 ? (int)b.window : 0;
     p.scale_log2 = scale * 1.4426950408889634f;
+    p.wait_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
     p.q = q;
     p.out = out;
     p.plan = reinterpret_cast<int32_t*>(w + wl.plan);
@@ -990,6 +1185,9 @@ static int paged_attention(const cx_pool* pool, int64_t layer, const cx_attn_bat
     if (rc) return rc;
     rc = make_pool_tmap(&tv, pool->v, pool, sh.hg);
     if (rc) return rc;
+    if (use_f32)
+        return pool->head_dim == 128 ? launch_f32_d<128>(sh, tk, tv, p, st, grid)
+                                     : launch_f32_d<64>(sh, tk, tv, p, st, grid);
     if (pool->head_dim == 128)
         return q_dtype == CX_F32 ? launch_mma_d<128, float>(sh, tk, tv, p, st, grid)
                                  : launch_mma_d<128, __nv_bfloat16>(sh, tk, tv, p, st, grid);
@@ -1006,7 +1204,8 @@ size_t cx_paged_workspace_bytes(const cx_pool* pool, const cx_attn_batch* b) {
     if (!pool || !b || pool->n_kv_heads <= 0 || b->n_q_heads <= 0 || b->batch < 0) return 0;
     const int64_t G = b->n_q_heads / pool->n_kv_heads;
     const int64_t max_q = b->q_start ? (b->max_q_len > 0 ? b->max_q_len : 1) : 1;
-    return ws_layout(b->batch, pool->n_kv_heads, G * max_q, pool->head_dim, grid_size()).total;
+    return ws_layout(b->batch, unit_shape(pool, G * max_q), G * max_q, pool->head_dim,
+                     grid_size()).total;
 }
 
 int cx_paged_kernel_kind(const cx_pool* pool, const cx_attn_batch* batch, int32_t q_dtype,
@@ -1017,7 +1216,12 @@ int cx_paged_kernel_kind(const cx_pool* pool, const cx_attn_batch* batch, int32_
     b.max_q_len = verify ? (b.max_q_len > 0 ? b.max_q_len : 1) : 1;
     if (tc_eligible(pool, &b, q_dtype)) return CX_KERNEL_TCGEN05;
     if (mma_eligible(pool, &b, q_dtype)) return CX_KERNEL_MMA;
+    if (f32_eligible(pool, &b, q_dtype)) return CX_KERNEL_FMA;
     return CX_KERNEL_GENERIC;
+}
+
+void cx_set_wait_limit_ns(uint64_t ns) {
+    cx::g_wait_limit_ns.store(ns ? ns : cx::kWaitLimitNs, std::memory_order_relaxed);
 }
 
 int cx_paged_decode(const cx_pool* pool, int64_t layer, const cx_attn_batch* batch, const void* q,

@@ -62,7 +62,8 @@ extern "C" int cx_paged_decode_static(const cx_pool* pool, int64_t layer,
                                       int32_t q_dtype, float* out, void* stream) {
     using namespace cx;
     if (!pool || !batch) return fail(CX_ERR_SHAPE, "cx_paged_decode_static: NULL pool or batch");
-    const size_t need = cx_paged_workspace_bytes(pool, batch);
+    // only the split-K kernels use scratch (the generic kernel needs none)
+    const size_t need = paged_scratch_need(pool, batch, q, q_dtype, out, false);
     if (need > kScratchBytes)
         return fail(CX_ERR_WORKSPACE,
                     "cx_paged_decode_static: this batch needs " + std::to_string(need) +

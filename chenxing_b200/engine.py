@@ -36,6 +36,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
+from ._arrays import upload
 from .batch import PagedBatch, slot_mapping
 from .radix_kv import RadixPagedKVCache
 
@@ -221,8 +222,8 @@ class BatchedKVEngine:
         c = self.cache
         dev = c.device
         bs = c.block_size
-        p.slots = torch.from_numpy(
-            slot_mapping([s.block_table for s in p.seqs], p.n_past, p.q_lens, bs)).to(dev)
+        p.slots = upload(slot_mapping([s.block_table for s in p.seqs], p.n_past, p.q_lens, bs),
+                         dev)
         if attend:
             is_verify = bool(np.any(p.q_lens != 1)) if verify is None else verify
             p.batch = PagedBatch(c, [s.block_table for s in p.seqs], p.n_past + p.q_lens,
@@ -231,7 +232,7 @@ class BatchedKVEngine:
                                  window=self.window, scale=self.scale)
         if p.cow_host:
             arr = np.asarray(p.cow_host, dtype=np.int32).T.copy()
-            p.cow = tuple(torch.from_numpy(a).to(dev) for a in arr)
+            p.cow = tuple(upload(a, dev) for a in arr)
         return p
 
     def plan_host(self, seq_ids, q_lens=None) -> StepPlan:
@@ -293,7 +294,7 @@ class BatchedKVEngine:
             pos = np.concatenate([np.arange(n0, n0 + n, dtype=np.int64)
                                   for n0, n in zip(plan.n_past, plan.q_lens)]) \
                 if len(plan.q_lens) else np.zeros(0, dtype=np.int64)
-            plan.positions = torch.from_numpy(pos).to(self.cache.device)
+            plan.positions = upload(pos, self.cache.device)
         qo = self.cache.append_rope(layer, k, v, plan.slots, plan.positions, rope, q,
                                     q_out_dtype)
         plan.appended.add(int(layer))

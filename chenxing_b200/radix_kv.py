@@ -30,7 +30,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._arrays import to_device, to_numpy, torch_dtype
+from ._arrays import to_device, to_numpy, torch_dtype, upload
 
 __all__ = ["RadixPagedKVCache", "RadixIndex", "PrefixHit", "OutOfKVCacheError"]
 
@@ -332,7 +332,7 @@ class RadixPagedKVCache(RadixIndex):
         shape = (t_total, self.n_kv_heads, self.head_dim)
         if tuple(kt.shape) != shape or tuple(vt.shape) != shape:
             raise ValueError(f"k/v must have shape {shape}, got {tuple(kt.shape)} / {tuple(vt.shape)}")
-        st = torch.from_numpy(slots).to(self.device)
+        st = upload(slots, self.device)
         self.append_slots(layer, kt, vt, st)
 
     def append_slots(self, layer: int, k: torch.Tensor, v: torch.Tensor,
@@ -388,8 +388,8 @@ class RadixPagedKVCache(RadixIndex):
         if len(set(dst)) != len(dst) or set(src) & set(dst):
             raise ValueError("copy_blocks needs distinct destinations disjoint from sources")
         n_slots = self.block_size if n_slots is None else int(n_slots)
-        s = torch.tensor(src, dtype=torch.int32, device=self.device)
-        t = torch.tensor(dst, dtype=torch.int32, device=self.device)
+        s = upload(np.asarray(src, dtype=np.int32), self.device)
+        t = upload(np.asarray(dst, dtype=np.int32), self.device)
         _lib.check(_lib.lib().cx_block_copy(self._pool, s.data_ptr(), t.data_ptr(), len(src),
                                             n_slots, _lib.stream_ptr(self.device)),
                    "cx_block_copy")

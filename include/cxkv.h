@@ -181,11 +181,14 @@ int cx_paged_verify(const cx_pool* pool, int64_t layer, const cx_attn_batch* bat
  * already fully reserved by the block pool and its own allocator, or a host
  * runtime behind a plain C FFI with no device allocator to give us.
  * - Rejects, with CX_ERR_WORKSPACE and a message, any batch whose scratch
- *   need (cx_paged_workspace_bytes) exceeds 8 MiB; it never calls cudaMalloc,
+ *   need (cx_paged_workspace_bytes, for the split-K kernels; batches that take
+ *   the generic kernel need none) exceeds 8 MiB; it never calls cudaMalloc,
  *   cudaFree or any allocating library routine.
  * - The first call on a device resolves the scratch address with
  *   cudaGetSymbolAddress (that device must be current); make that first call
- *   before any stream capture.
+ *   before any stream capture.  The address is cached per device index for
+ *   the life of the process: after cudaDeviceReset on a device it is stale,
+ *   so do not call this entry point on that device again in the process.
  * - Every call re-plans and zeroes the merge tickets itself.  All calls on a
  *   device share the one scratch array, which keeps the last call's contents:
  *   calls that overlap on the GPU (different streams, no ordering between
@@ -193,16 +196,28 @@ int cx_paged_verify(const cx_pool* pool, int64_t layer, const cx_attn_batch* bat
 int cx_paged_decode_static(const cx_pool* pool, int64_t layer, const cx_attn_batch* batch,
                            const void* q, int32_t q_dtype, float* out, void* stream);
 
+/* Limit, in nanoseconds, of every pipeline wait inside the decode / verify
+ * kernels of later calls in this process (0 restores the default, 2 s).  A
+ * wait that runs out makes its CTA stop, wait (with the default limit) for its
+ * own copies in flight, raise CX_DEV_WAIT_TIMEOUT and return; that call's
+ * output is then undefined and the device stays usable.  Meant for tests of
+ * that failure path (a limit of a few nanoseconds makes the waits run out);
+ * no counterpart in the reference, which has no device waits. */
+void cx_set_wait_limit_ns(uint64_t ns);
+
 /* Which kernel cx_paged_decode (verify = 0) or cx_paged_verify (verify = 1)
  * runs for this pool, batch shape and query type — diagnostics, no
- * counterpart in the reference: CX_KERNEL_GENERIC (fp32 / fp16 pools, other
- * block sizes or head dims: exact CUDA-core kernel), CX_KERNEL_MMA (bf16
- * pool, packed query tile of 1..63 rows: TMA + mma.sync split-K kernel) or
- * CX_KERNEL_TCGEN05 (bf16 pool, packed tile of 64 rows or more: TMA +
- * tcgen05 / TMEM kernel).  Reads only the host fields of `batch` and assumes
+ * counterpart in the reference: CX_KERNEL_GENERIC (fp16 pools, other block
+ * sizes or head dims, fp32 pools beyond 64 packed rows: exact CUDA-core
+ * kernel), CX_KERNEL_MMA (bf16 pool, packed query tile of 1..63 rows: TMA +
+ * mma.sync split-K kernel), CX_KERNEL_TCGEN05 (bf16 pool, packed tile of 64
+ * rows or more: TMA + tcgen05 / TMEM kernel) or CX_KERNEL_FMA (fp32 pool,
+ * 16-token blocks, head_dim 64 / 128, up to 64 packed rows per KV head: TMA +
+ * fp32 FMA split-K kernel).  Packed rows = (n_q_heads / n_kv_heads) x
+ * max_q_len.  Reads only the host fields of `batch` and assumes
  * 16-byte-aligned q and out pointers: the decode / verify calls run the
  * generic kernel for q or out pointers that are not 16-byte aligned. */
-enum { CX_KERNEL_GENERIC = 0, CX_KERNEL_MMA = 1, CX_KERNEL_TCGEN05 = 2 };
+enum { CX_KERNEL_GENERIC = 0, CX_KERNEL_MMA = 1, CX_KERNEL_TCGEN05 = 2, CX_KERNEL_FMA = 3 };
 int cx_paged_kernel_kind(const cx_pool* pool, const cx_attn_batch* batch, int32_t q_dtype,
                          int32_t verify);
 

@@ -4,6 +4,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from conftest import record_margin
 from oracle.attention import CausalMask, flash_attention, naive_attention
 
 BF16_RTOL = 2e-2     # bf16 pools: max|out - ref| <= 2e-2 * max|ref| per sequence
@@ -91,7 +92,8 @@ class PagedCase:
         return outs
 
     def check(self, out, atol=None, rtol=None):
-        """Compare per sequence; returns the worst normalised error."""
+        """Compare per sequence; returns the worst normalised error (error /
+        bound), which the terminal summary also reports per test."""
         refs = self.oracle()
         worst, qo = 0.0, 0
         for b, ref in enumerate(refs):
@@ -108,6 +110,7 @@ class PagedCase:
                 assert err <= bound + 1e-30, \
                     f"seq {b} ctx {self.ctx[b]}: max abs err {err} > {rtol} * {scale}"
                 worst = max(worst, err / bound if bound > 0 else 0.0)
+        record_margin(worst)
         return worst
 
 
@@ -142,7 +145,9 @@ def assert_close_rows(got, ref, rtol=BF16_RTOL, what=""):
     err = float(np.abs(got - ref).max())
     bound = rtol * float(np.abs(ref).max())
     assert err <= bound, f"{what}: max abs err {err} > {bound}"
-    return err / bound if bound else 0.0
+    worst = err / bound if bound else 0.0
+    record_margin(worst)
+    return worst
 
 
 def claim_blocks(index, ids):

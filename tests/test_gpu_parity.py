@@ -159,6 +159,7 @@ def test_cfg1_decode_run_matches_reference_golden():
         cache.append_batch(0, data["k"][s], data["v"][s], slots)
         ctx += 1
         batch = PagedBatch(cache, wl.block_tables, ctx, n_q_heads=wl.n_q_heads)
+        assert batch.kernel_kind(torch.float32) == "fma"
         out = cache.decode_batch(0, data["q"][s], batch).cpu().numpy()
         key = f"out_step{s}"
         if key in g.files:
@@ -370,23 +371,62 @@ def test_tcgen05_row_max_jump_mid_sequence():
 
 def test_kernel_selection_by_packed_rows():
     """Decode and short verify chains (< 64 packed rows) stay on the split-K
-    mma.sync kernel; 64 rows and more go to tcgen05; fp32 pools stay on the
-    exact generic kernel."""
+    mma.sync kernel; 64 rows and more go to tcgen05; fp32 pools take the fp32
+    FMA kernel up to 64 packed rows and the exact generic kernel beyond."""
     dec = PagedCase(hq=32, hk=8, d=128, ctx=[100], seed=1)
     assert dec.batch().kernel_kind() == "mma"
     short = PagedCase(hq=32, hk=8, d=128, ctx=[100], q_lens=[15], seed=1)
     assert short.batch().kernel_kind() == "mma"
     edge = PagedCase(hq=32, hk=8, d=128, ctx=[100], q_lens=[16], seed=1)
     assert edge.batch().kernel_kind() == "tcgen05"
-    f32 = PagedCase(hq=32, hk=8, d=128, ctx=[100], q_lens=[64], dtype=np.float32, seed=1)
+    f32 = PagedCase(hq=32, hk=8, d=128, ctx=[100], q_lens=[16], dtype=np.float32, seed=1)
+    assert f32.batch().kernel_kind() == "fma"
+    f32 = PagedCase(hq=32, hk=8, d=128, ctx=[100], q_lens=[17], dtype=np.float32, seed=1)
     assert f32.batch().kernel_kind() == "generic"
 
 
 def test_fp32_pool_paged_decode_and_verify_exact():
     case = PagedCase(hq=8, hk=2, d=64, ctx=[64, 511, 1, 130], dtype="float32", seed=1)
+    assert case.batch().kernel_kind(torch.float32) == "fma"
     case.check(case.run(), atol=F32_ATOL)
     case = PagedCase(hq=8, hk=2, d=64, ctx=[64, 511, 9, 130], q_lens=[5, 5, 9, 1],
                      dtype="float32", window=50, seed=2)
+    case.check(case.run(), atol=F32_ATOL)
+
+
+# fp32 pools on the TMA + FMA split-K kernel: the reference's own precision,
+# max |out - ref| <= 1e-5 against the oracle
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("hq,hk", [(32, 8), (8, 8), (16, 2), (8, 1)])
+@pytest.mark.parametrize("q_dtype", [torch.float32, torch.bfloat16])
+def test_fp32_decode_fma_kernel_matches_oracle(d, hq, hk, q_dtype):
+    ctx = [1, 15, 16, 17, 300, 2049, 5000, 0, 64]
+    case = PagedCase(hq=hq, hk=hk, d=d, ctx=ctx, dtype="float32", seed=d + hq + hk,
+                     q_dtype=q_dtype)
+    assert case.batch().kernel_kind(q_dtype) == "fma"
+    case.check(case.run(), atol=F32_ATOL)
+
+
+@pytest.mark.parametrize("q_lens,window", [([1, 4, 9, 16], None), ([16, 16, 3, 1], 40),
+                                           ([2, 7, 13, 8], 4096), ([5, 1, 16, 11], 1)])
+@pytest.mark.parametrize("d", [64, 128])
+def test_fp32_verify_fma_kernel_matches_oracle(q_lens, window, d):
+    """Packed tiles of 4 to 64 rows (row tiles of 4, 8 and 16 rows, up to four
+    of them), ragged query lengths, causal within the draft and windows."""
+    ctx = [700, 65, 3000, 16]
+    case = PagedCase(hq=16, hk=4, d=d, ctx=ctx, q_lens=q_lens, dtype="float32", window=window,
+                     seed=len(q_lens) * 7 + d)
+    assert case.batch().kernel_kind(torch.float32) == "fma"
+    case.check(case.run(), atol=F32_ATOL)
+
+
+def test_fp32_decode_long_contexts_split_across_ctas():
+    """Long fp32 contexts cut by CTA chunk boundaries (ticket merge of partial
+    softmax states), cfg2-shaped heads."""
+    rng = np.random.default_rng(11)
+    ctx = rng.integers(1024, 20000, size=12)
+    case = PagedCase(hq=32, hk=8, d=128, ctx=ctx, dtype="float32", seed=11,
+                     q_scale=1 / np.sqrt(128), kv_scale=1.0)
     case.check(case.run(), atol=F32_ATOL)
 
 
@@ -473,6 +513,64 @@ def test_device_range_checks_raise_flags():
     b.block_tables[0, 1] = 9                      # bypass host validation
     c.decode_batch(0, torch.zeros((1, 32, 128), device="cuda"), b)
     assert _lib.device_flags(clear=True) & 2
+
+
+@pytest.mark.parametrize("dtype,hk,d", [("bfloat16", 8, 128), ("bfloat16", 2, 64),
+                                        (np.float32, 2, 64)])
+def test_bad_block_id_leaves_its_keys_out(dtype, hk, d):
+    """A block id outside the pool raises CX_DEV_BAD_BLOCK and that block's
+    keys are left out: the output equals attention over the other keys only
+    (the bad block's ring stage holds no data and must not be computed on)."""
+    from chenxing_b200 import _lib
+    from gpu_cases import oracle_rows
+    hq = 4 * hk
+    case = PagedCase(hq=hq, hk=hk, d=d, ctx=[40, 33], dtype=dtype, seed=5, spare_blocks=0)
+    batch = case.batch()
+    kind = batch.kernel_kind(case.q_dev.dtype)
+    batch.block_tables[0, 1] = case.cache.n_blocks + 3     # keys 16..31 of sequence 0
+    out = case.run(batch)
+    assert _lib.device_flags(clear=True) & 2, kind
+    keep = np.r_[0:16, 32:40]
+    q0 = case.q[0:1]
+    ref0 = oracle_rows(q0, case.k[keep], case.v[keep])
+    tol = dict(rtol=BF16_RTOL) if dtype == "bfloat16" else {}
+    if dtype == "bfloat16":
+        from gpu_cases import assert_close_rows
+        assert_close_rows(out[0:1], ref0, what=f"bad block, {kind}")
+    else:
+        assert np.abs(out[0:1] - ref0).max() <= F32_ATOL, kind
+    # the other sequence is untouched
+    ref1 = case.oracle()[1]
+    if tol:
+        assert np.abs(out[1:2] - ref1).max() <= BF16_RTOL * np.abs(ref1).max()
+    else:
+        assert np.abs(out[1:2] - ref1).max() <= F32_ATOL
+
+
+def test_wait_timeout_returns_with_flag_and_next_call_is_clean():
+    """The decode kernel's bounded pipeline waits: with a limit of a few
+    nanoseconds the waits run out, the call still returns, CX_DEV_WAIT_TIMEOUT
+    is raised and the context stays usable; with the default limit restored the
+    same batch is parity-green again (cfg2 shape: 64 sequences, 1k-8k keys)."""
+    from chenxing_b200 import _lib
+    rng = np.random.default_rng(3)
+    ctx = rng.integers(1024, 8193, size=64)
+    case = PagedCase(hq=32, hk=8, d=128, ctx=ctx, seed=3, q_scale=1 / np.sqrt(128),
+                     kv_scale=1 / np.sqrt(128))
+    batch = case.batch()
+    assert batch.kernel_kind(case.q_dev.dtype) == "mma"
+    lib = _lib.lib()
+    try:
+        lib.cx_set_wait_limit_ns(5)
+        case.run(batch)                     # returns (bounded waits), output undefined
+        flags = _lib.device_flags(clear=True)
+    finally:
+        lib.cx_set_wait_limit_ns(0)         # default limit again
+    assert flags & 8, f"expected a wait timeout, flags = {_lib.describe_flags(flags)}"
+    batch.needs_plan = True
+    out = case.run(batch)
+    assert _lib.device_flags(clear=True) == 0
+    case.check(out, rtol=BF16_RTOL)
 
 
 # ---------------------------------------------------------------------------

@@ -37,9 +37,11 @@ def test_kernel_selection_rules_read_host_fields_only():
     """cx_paged_kernel_kind decides from host fields alone, so the dispatch
     rules hold without a GPU: bf16 pools with 16-token blocks and head_dim 64 /
     128 take mma.sync below 64 packed rows (query tokens x GQA group) and
-    tcgen05 from 64 rows; fp32 / fp16 pools, other block sizes or head dims
-    and pools not 16-byte aligned take the generic kernel.  The pool and
-    table addresses are placeholders that nothing dereferences."""
+    tcgen05 from 64 rows; fp32 pools with 16-token blocks and head_dim 64 /
+    128 take the fp32 FMA kernel up to 64 packed rows; fp16 pools, other
+    block sizes or head dims, longer fp32 query tiles and pools not 16-byte
+    aligned take the generic kernel.  The pool and table addresses are
+    placeholders that nothing dereferences."""
     lib = _lib.load_library()
 
     def kind(*, dtype=_lib.CX_BF16, bs=16, d=128, hk=8, hq=32, q=1, verify=1,
@@ -57,8 +59,14 @@ def test_kernel_selection_rules_read_host_fields_only():
     assert kind(hq=8, hk=8, q=63) == "mma" and kind(hq=8, hk=8, q=64) == "tcgen05"
     assert kind(q=200, q_dtype=_lib.CX_F32) == "tcgen05"
     assert kind(q=200, q_dtype=_lib.CX_F16) == "generic"
-    for bad in (dict(dtype=_lib.CX_F32), dict(dtype=_lib.CX_F16), dict(bs=32), dict(d=96),
-                dict(d=256), dict(base=0x100008)):
+    f32 = dict(dtype=_lib.CX_F32)
+    assert kind(verify=0, **f32) == kind(verify=0, d=64, **f32) == "fma"
+    assert kind(q=16, **f32) == "fma" and kind(q=17, **f32) == "generic"   # 64 / 68 rows
+    assert kind(q=4, q_dtype=_lib.CX_F32, **f32) == "fma"
+    assert kind(q=4, q_dtype=_lib.CX_F16, **f32) == "generic"
+    for bad in (dict(dtype=_lib.CX_F16), dict(bs=32), dict(d=96), dict(d=256),
+                dict(base=0x100008), dict(dtype=_lib.CX_F32, bs=8),
+                dict(dtype=_lib.CX_F32, d=32), dict(dtype=_lib.CX_F32, base=0x100008)):
         assert kind(**bad) == "generic", bad
         assert kind(q=100, **bad) == "generic", bad
 
