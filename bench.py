@@ -39,6 +39,18 @@ ELEM = 2  # bf16
 UNIT_BYTES = 2 * HK * D * ELEM  # K + V bytes per KV token-layer
 
 
+_SINK = None     # list collecting the secondary modes' lines in the default run
+
+
+def emit(line):
+    """Print a mode's JSON line, or keep it for the default line's
+    ``secondary`` block when the default run collects them."""
+    if _SINK is not None:
+        _SINK.append(line)
+    else:
+        print(json.dumps(line), flush=True)
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -47,7 +59,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["cfg2", "small", "prefill", "prefill-small",
                                          "prefill-d64", "append", "cfg4", "cfg4-small",
-                                         "copy", "cfg1", "cfg2-f32", "cfg5"],
+                                         "copy", "cfg1", "cfg2-f32", "cfg5", "cfg3"],
                     default="cfg2",
                     help="small: 1 layer, pool sized to need (~2 GB, for profiler captures); "
                          "prefill: chunked-prefill attention on the tcgen05 kernel (its own "
@@ -63,13 +75,18 @@ def parse():
                          "on an fp32 pool (GB/s); cfg5: continuous-batching churn, one "
                          "shard of 1024 lognormal sequences per GPU (run under torchrun)")
     ap.add_argument("--pool-frac", type=float, default=0.9)
-    ap.add_argument("--layers", type=int, default=32, help="cfg5: layers per step")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="cfg5 / cfg2-f32: layers per step (default 32 / 8)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="cfg2-f32: sequences (default 64; fewer for profiler captures)")
     ap.add_argument("--gather", choices=["serial", "overlap"], default="serial",
                     help="N > 1: all-gather of each step's rows on the step stream after "
                          "its last layer (serial), or on a side stream overlapped with the "
                          "next step (overlap)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="default run: skip the other configurations' lines")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--gamma", type=int, choices=[0, 4, 8], default=0,
@@ -548,10 +565,13 @@ def run_ours(args):
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "allgather_ms_per_step": ag_ms,
                 "gpu_launches": timed_launches, "clocks": clocks}
+        if world == 1:
+            return line
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+    return None
 
 
 def run_e2e(args, lib, pool, cache, batches, slots, layers, n_sets, dev, world, units_step,
@@ -736,7 +756,7 @@ def run_prefill(args):
                          "flops_per_launch": flops, "avg_launch_ms": avg,
                          "min_launch_ms": float(np.min(ms))},
             "clocks": clocks}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -779,11 +799,15 @@ def run_append(args):
     torch.cuda.synchronize(dev)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
+    sampler = ClockSampler(device_uuid(dev))
+    sampler.start()
+    time.sleep(0.5)
     for e0, e1 in evs:
         e0.record(stream)
         launch()
         e1.record(stream)
     torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
     if _lib.device_flags(clear=True):
         raise RuntimeError("device flags raised during the append bench")
     ms = [a.elapsed_time(b) for a, b in evs]
@@ -791,7 +815,7 @@ def run_append(args):
     alg = 2 * (2 * n_tok * HK * D * ELEM) + 8 * n_tok
     gbs = alg / (avg / 1e3) / 1e9
     peak, kind = measured_peak()
-    print(json.dumps({
+    emit({
         "metric": "KV append GB/s (cx_kv_append, prefill-sized)", "value": gbs, "unit": "GB/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": avg,
         "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16",
@@ -801,7 +825,8 @@ def run_append(args):
                    "l2": "2.1 GB moved per launch, > 126 MB L2"},
         "roofline": {"bound": "hbm", "kernel": "kv_append_vec_kernel", "achieved": gbs,
                      "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_source": kind,
-                     "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg}}), flush=True)
+                     "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg},
+        "clocks": clocks})
 
     # the same append with RoPE fused (cx_kv_append_rope): K rotated into the
     # pool, V copied, Q of Hq heads rotated into a bf16 q_out
@@ -822,11 +847,15 @@ def run_append(args):
     for _ in range(args.warmup):
         launch_rope()
     torch.cuda.synchronize(dev)
+    sampler = ClockSampler(device_uuid(dev))
+    sampler.start()
+    time.sleep(0.5)
     for e0, e1 in evs:
         e0.record(stream)
         launch_rope()
         e1.record(stream)
     torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
     if _lib.device_flags(clear=True):
         raise RuntimeError("device flags raised during the RoPE append bench")
     avg = float(np.mean([a.elapsed_time(b) for a, b in evs]))
@@ -834,7 +863,7 @@ def run_append(args):
     # rows are read once per token from cache, 1 KB per token)
     alg = 2 * (2 * n_tok * HK * D * ELEM) + 2 * n_tok * HQ * D * ELEM + 16 * n_tok
     gbs = alg / (avg / 1e3) / 1e9
-    print(json.dumps({
+    emit({
         "metric": "KV append with fused RoPE GB/s (cx_kv_append_rope, prefill-sized)",
         "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": avg, "higher_is_better": True, "scaling": "none",
@@ -842,9 +871,10 @@ def run_append(args):
         "config": {"workload": f"{B} sequences x {T} tokens, K / V appended and Q rotated "
                                f"({HQ} heads), blocks scattered",
                    "kv_heads": HK, "q_heads": HQ, "head_dim": D, "block_size": BS},
-        "roofline": {"bound": "hbm", "kernel": "kv_append_rope_kernel", "achieved": gbs,
+        "roofline": {"bound": "hbm", "kernel": "kv_append_rope_vec_kernel", "achieved": gbs,
                      "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_source": kind,
-                     "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg}}), flush=True)
+                     "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg},
+        "clocks": clocks})
 
 
 # ---------------------------------------------------------------------------
@@ -875,18 +905,24 @@ def run_copy(args):
         torch.cuda.synchronize(dev)
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]
+        sampler = ClockSampler(device_uuid(dev))
+        sampler.start()
+        time.sleep(0.5)
         for e0, e1 in evs:
             e0.record(stream)
             launch()
             e1.record(stream)
         torch.cuda.synchronize(dev)
+        clocks[0] = sampler.stop()
         if _lib.device_flags(clear=True):
             raise RuntimeError("device flags raised during the copy bench")
         return float(np.mean([a.elapsed_time(b) for a, b in evs]))
 
+    clocks = [None]
+
     def line(metric, kernel, alg, avg, workload):
         gbs = alg / (avg / 1e3) / 1e9
-        print(json.dumps({
+        emit({
             "metric": metric, "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": avg, "higher_is_better": True,
             "scaling": "none", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -894,7 +930,8 @@ def run_copy(args):
                        "l2": "> 126 MB moved per launch"},
             "roofline": {"bound": "hbm", "kernel": kernel, "achieved": gbs, "peak": peak,
                          "unit": "GB/s", "frac": gbs / peak, "peak_source": kind,
-                         "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg}}), flush=True)
+                         "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg},
+            "clocks": clocks[0]})
 
     # compaction: 8192 block moves over 4 layers
     L, NB, n = 4, 32768, 8192
@@ -994,12 +1031,16 @@ def run_verify(args):
         for _ in range(args.warmup):
             step(False)
         torch.cuda.synchronize(dev)
+        sampler = ClockSampler(device_uuid(dev))
+        sampler.start()
+        time.sleep(0.5)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(args.steps):
             step(True)
         end.record(stream)
         torch.cuda.synchronize(dev)
+        clocks = sampler.stop()
         if _lib.device_flags(clear=True):
             raise RuntimeError("device flags raised during the verify bench")
         ms = start.elapsed_time(end) / args.steps
@@ -1007,7 +1048,7 @@ def run_verify(args):
         alg = batch.kv_tokens * UNIT_BYTES + B * T * HQ * D * (ELEM + 4) + \
             4 * sum(len(t) for t in wl.block_tables)
         gbs = alg / (vms / 1e3) / 1e9
-        print(json.dumps({
+        emit({
             "metric": f"speculative-verify KV tokens/s (windowed key-layers/s, cfg4 gamma={gamma})",
             "value": units / (ms / 1e3), "unit": "KV-token-layers/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -1019,7 +1060,8 @@ def run_verify(args):
             "roofline": {"bound": "hbm", "kernel": "paged_attn_mma_kernel (verify)",
                          "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "peak_source": kind, "algorithmic_bytes_per_launch": alg,
-                         "avg_launch_ms": vms}}), flush=True)
+                         "avg_launch_ms": vms},
+            "clocks": clocks})
         del cache, q, kn, out
         torch.cuda.empty_cache()
 
@@ -1061,11 +1103,11 @@ def run_cfg1(args):
     out = torch.empty((steps, B, wl.n_q_heads, wl.head_dim), dtype=torch.float32, device=dev)
     lib, pool = _lib.lib(), cache.cx_pool()
     stream = torch.cuda.current_stream(dev)
-    sp = stream.cuda_stream
     units = int(sum((ctx0 + s + 1).sum() for s in range(steps)))
     dec_ev = []
 
     def run(timed):
+        sp = torch.cuda.current_stream(dev).cuda_stream     # the capture stream in a graph
         for s in range(steps):
             bt = batches[s]
             _lib.check(lib.cx_kv_append(pool, 0, k[s].data_ptr(), v[s].data_ptr(), _lib.CX_F32,
@@ -1090,7 +1132,26 @@ def run_cfg1(args):
         run(False)
     end.record(stream)
     torch.cuda.synchronize(dev)
+    eager_ms = start.elapsed_time(end) / args.steps
+    # the same 32-step run as one CUDA graph (96 launches: append, plan and
+    # decode per step), replayed: no host launch cost between the kernels
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+        run(False)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(device_uuid(dev))
+    sampler.start()
+    time.sleep(0.5)
+    start.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
     ms = start.elapsed_time(end) / args.steps
+    del graph
     run(True)                                  # per-launch decode times, one extra run
     torch.cuda.synchronize(dev)
     if _lib.device_flags(clear=True):
@@ -1102,11 +1163,13 @@ def run_cfg1(args):
     cpu = None
     if not args.no_cpu_baseline:
         cpu = cpu_cfg1_rate(args.seed)
-    print(json.dumps({
+    emit({
         "metric": "cfg1 paged-decode KV tokens/s (fp32 pool, 32-step run of append + decode)",
         "value": units / (ms / 1e3), "unit": "KV-token-layers/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "ms_per_decode_step": ms / steps, "higher_is_better": True, "scaling": "none",
+        "ms_per_decode_step": ms / steps, "eager_ms_per_step": eager_ms,
+        "launch": "CUDA graph of the 32-step run (eager launches: eager_ms_per_step)",
+        "gpu_launches": 3 * steps * args.steps, "higher_is_better": True, "scaling": "none",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (cfg1 seeded N(0,1) Q/K/V)",
         "config": {"workload": "cfg1: 8 seqs, ctx U[64,512], Hq 8 / Hkv 2, D 64, fp32, "
                                "32 decode steps per timed step", "kernel": kind,
@@ -1115,7 +1178,7 @@ def run_cfg1(args):
                      "avg_launch_ms": dms, "algorithmic_bytes_per_launch": alg,
                      "achieved": alg / (dms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": alg / (dms / 1e3) / 1e9 / peak, "peak_source": pk},
-        "cpu_baseline": cpu}), flush=True)
+        "cpu_baseline": cpu, "clocks": clocks})
 
 
 def cpu_cfg1_rate(seed):
@@ -1162,9 +1225,10 @@ def run_f32_decode(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    layers, steps_total = 8, args.warmup + args.steps
-    n_blocks = BATCH * (-(-(8192 + steps_total) // BS)) + 64
-    wl = cfg2_meta(n_blocks=n_blocks, seed=args.seed, batch=BATCH, steps=steps_total,
+    layers, steps_total = args.layers or 8, args.warmup + args.steps
+    nb_seq = args.batch or BATCH
+    n_blocks = nb_seq * (-(-(8192 + steps_total) // BS)) + 64
+    wl = cfg2_meta(n_blocks=n_blocks, seed=args.seed, batch=nb_seq, steps=steps_total,
                    n_layers=layers)
     cache = RadixPagedKVCache(n_blocks, BS, layers, HK, D, dtype=np.float32, device=dev,
                               host_io=False)
@@ -1175,13 +1239,13 @@ def run_f32_decode(args):
             t[l].normal_(0.0, 1.0 / math.sqrt(D), generator=g)
     ctx0 = wl.ctx_lens.astype(np.int64)
     sc = 1.0 / math.sqrt(D)
-    q = torch.randn((layers, BATCH, HQ, D), device=dev, generator=g) * sc
-    kn = torch.randn((layers, BATCH, HK, D), device=dev, generator=g) * sc
-    out = torch.empty((BATCH, HQ, D), dtype=torch.float32, device=dev)
+    q = torch.randn((layers, nb_seq, HQ, D), device=dev, generator=g) * sc
+    kn = torch.randn((layers, nb_seq, HK, D), device=dev, generator=g) * sc
+    out = torch.empty((nb_seq, HQ, D), dtype=torch.float32, device=dev)
     stride = max(len(t) for t in wl.block_tables)
     batches = [PagedBatch(cache, wl.block_tables, ctx0 + s + 1, n_q_heads=HQ,
                           table_stride=stride) for s in range(steps_total)]
-    slots = [torch.from_numpy(slot_mapping(wl.block_tables, ctx0 + s, [1] * BATCH, BS)).to(dev)
+    slots = [torch.from_numpy(slot_mapping(wl.block_tables, ctx0 + s, [1] * nb_seq, BS)).to(dev)
              for s in range(steps_total)]
     kind = batches[0].kernel_kind(torch.float32)
     lib, pool = _lib.lib(), cache.cx_pool()
@@ -1193,7 +1257,7 @@ def run_f32_decode(args):
         bt = batches[s]
         for l in range(layers):
             _lib.check(lib.cx_kv_append(pool, l, kn[l].data_ptr(), kn[l].data_ptr(), _lib.CX_F32,
-                                        slots[s].data_ptr(), BATCH, None, None, None, 0, sp),
+                                        slots[s].data_ptr(), nb_seq, None, None, None, 0, sp),
                        "cx_kv_append")
             if timed:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
@@ -1226,29 +1290,189 @@ def run_f32_decode(args):
     dms = float(np.mean([a.elapsed_time(b) for a, b, _ in dec_ev]))
     kv_tok = float(np.mean([int((ctx0 + s + 1).sum()) for _, _, s in dec_ev]))
     nblk = sum(len(t) for t in wl.block_tables)
-    alg = kv_tok * 2 * HK * D * 4 + BATCH * HQ * D * 8 + 4 * nblk
+    alg = kv_tok * 2 * HK * D * 4 + nb_seq * HQ * D * 8 + 4 * nblk
     gbs = alg / (dms / 1e3) / 1e9
     peak, pk = measured_peak()
-    print(json.dumps({
+    emit({
         "metric": "paged-decode KV tokens/s, fp32 pool (cfg2 shape)",
         "value": units / (ms / 1e3) , "unit": "KV-token-layers/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1)/sqrt(128) K/V/Q)",
-        "config": {"workload": f"cfg2 shape on an fp32 pool: 64 seqs, ctx U[1024,8192], "
+        "config": {"workload": f"cfg2 shape on an fp32 pool: {nb_seq} seqs, ctx U[1024,8192], "
                                f"{layers} layers per step (append + decode)", "kernel": kind,
                    "q_heads": HQ, "kv_heads": HK, "head_dim": D, "block_size": BS,
                    "l2": "K/V ~4.9 GB per decode launch, > 126 MB L2"},
         "roofline": {"bound": "hbm", "kernel": "paged_attn_f32_kernel", "achieved": gbs,
                      "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_source": pk,
                      "algorithmic_bytes_per_launch": alg, "avg_launch_ms": dms},
-        "clocks": clocks}), flush=True)
+        "clocks": clocks})
+
+
+# ---------------------------------------------------------------------------
+# cfg3: radix prefix sharing with copy-on-write of the shared tail (separate mode)
+# ---------------------------------------------------------------------------
+def run_cfg3(args):
+    """cfg3: 256 requests in 4 groups; each group shares a 2048-token prefix
+    (128 whole blocks found through the radix tree, refcount 64) plus a
+    partially filled tail block that all its requests alias; Hq 32 / Hkv 32,
+    D 128, bf16, 4 layers.  One step, per layer: the requests' suffixes
+    (~ U[128, 512] tokens each) appended with the 256 copy-on-write copies of
+    the tails fused into the same launch, then one decode token appended per
+    request and a paged decode over prefix + suffix + token.  Repeating the
+    step rewrites the same slots with the same data.  Units = KV token-layers
+    attended; the four shared prefixes (128 MB a layer) are read by 64
+    requests each, so the decode reads far fewer DRAM bytes than it attends."""
+    import torch
+    from chenxing_b200 import PagedBatch, RadixPagedKVCache, _lib
+    from chenxing_b200.batch import slot_mapping
+    from chenxing_b200.seqmeta import grow_table
+    from chenxing_b200.workloads import prefix_share_meta
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hk, hq, L = 32, 32, 4
+    meta_w = prefix_share_meta(seed=args.seed + 3)
+    P0, tails, suffix = meta_w["prefix_tokens"], meta_w["tail"], meta_w["suffix"]
+    G, R = suffix.shape
+    n_blocks = G * (P0 // BS + 1) + int(sum(-(-(int(t) + int(x) + 1) // BS) + 1
+                                            for t, row in zip(tails, suffix) for x in row)) + 64
+    cache = RadixPagedKVCache(n_blocks, BS, L, hk, D, dtype="bfloat16", device=dev,
+                              host_io=False)
+    rng = np.random.default_rng(args.seed + 3)
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 3)
+    sc = 1.0 / math.sqrt(D)
+    gtables, prefix_tok = [], []
+    for gi in range(G):                       # writers: prefix + tail, published
+        plen = P0 + int(tails[gi])
+        toks = [100000 * (gi + 1)] + rng.integers(0, 50000, size=plen - 1).tolist()
+        t = []
+        grow_table(cache, t, plen)
+        sl = slot_mapping([t], [0], [plen], BS)
+        for l in range(L):
+            kv = (torch.randn((2, plen, hk, D), device=dev, generator=g) * sc).bfloat16()
+            cache.append_batch(l, kv[0], kv[1], sl)
+        cache.insert(toks[:P0], t[:P0 // BS])
+        gtables.append(t)
+        prefix_tok.append(toks)
+    tables, n_past, cow = [], [], ([], [], [])
+    for gi in range(G):                       # requests: prefix hit + aliased tail + CoW
+        tail_id = gtables[gi][P0 // BS]
+        for ri in range(R):
+            prompt = prefix_tok[gi] + rng.integers(0, 50000, size=int(suffix[gi, ri])).tolist()
+            hit = cache.match_prefix(prompt)
+            cache.acquire(hit.node)
+            t = hit.block_ids + [tail_id]
+            dst = cache.alloc_block()
+            cow[0].append(tail_id)
+            cow[1].append(dst)
+            cow[2].append(int(tails[gi]))
+            t[P0 // BS] = dst
+            grow_table(cache, t, P0 + int(tails[gi]) + int(suffix[gi, ri]) + 1)
+            tables.append(t)
+            n_past.append(P0 + int(tails[gi]))
+    n_past = np.asarray(n_past, dtype=np.int64)
+    n_suf = suffix.reshape(-1).astype(np.int64)
+    B = len(tables)
+    refcnt = cache.match_prefix(prefix_tok[0]).node.refcnt
+    suf = (torch.randn((2, int(n_suf.sum()), hk, D), device=dev, generator=g) * sc).bfloat16()
+    dec = (torch.randn((2, B, hk, D), device=dev, generator=g) * sc).bfloat16()
+    q = (torch.randn((B, hq, D), device=dev, generator=g) * sc).bfloat16()
+    s1 = torch.from_numpy(slot_mapping(tables, n_past, n_suf, BS)).to(dev)
+    s2 = torch.from_numpy(slot_mapping(tables, n_past + n_suf, [1] * B, BS)).to(dev)
+    cow_t = tuple(torch.tensor(c, dtype=torch.int32, device=dev) for c in cow)
+    batch = PagedBatch(cache, tables, n_past + n_suf + 1, n_q_heads=hq)
+    out = torch.empty((B, hq, D), dtype=torch.float32, device=dev)
+    lib, pool = _lib.lib(), cache.cx_pool()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    c = batch.c_struct()
+    app_ev, dec_ev = [], []
+
+    def step(timed):
+        for l in range(L):
+            a0 = a1 = None
+            if timed:
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+                    enable_timing=True)
+                a0.record(stream)
+            _lib.check(lib.cx_kv_append(pool, l, suf[0].data_ptr(), suf[1].data_ptr(),
+                                        _lib.CX_BF16, s1.data_ptr(), int(n_suf.sum()),
+                                        cow_t[0].data_ptr(), cow_t[1].data_ptr(),
+                                        cow_t[2].data_ptr(), B, sp), "cx_kv_append")
+            if timed:
+                a1.record(stream)
+                app_ev.append((a0, a1))
+            _lib.check(lib.cx_kv_append(pool, l, dec[0].data_ptr(), dec[1].data_ptr(),
+                                        _lib.CX_BF16, s2.data_ptr(), B, None, None, None, 0, sp),
+                       "cx_kv_append")
+            if timed:
+                d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+                    enable_timing=True)
+                d0.record(stream)
+            _lib.check(lib.cx_paged_decode(pool, l, c, q.data_ptr(), _lib.CX_BF16, out.data_ptr(),
+                                           batch.workspace.data_ptr(), batch.workspace.numel(),
+                                           int(l == 0), sp), "cx_paged_decode")
+            if timed:
+                d1.record(stream)
+                dec_ev.append((d0, d1))
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(device_uuid(dev))
+    sampler.start()
+    time.sleep(0.5)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    if _lib.device_flags(clear=True):
+        raise RuntimeError("device flags raised during the cfg3 bench")
+    ms = start.elapsed_time(end) / args.steps
+    kv_tok = int(batch.ctx_host.sum())
+    units = kv_tok * L
+    ams = float(np.mean([a.elapsed_time(b) for a, b in app_ev]))
+    dms = float(np.mean([a.elapsed_time(b) for a, b in dec_ev]))
+    tok_bytes = 2 * hk * D * ELEM
+    app_alg = 2 * int(n_suf.sum()) * tok_bytes + 8 * int(n_suf.sum()) + \
+        2 * sum(cow[2]) * tok_bytes
+    dec_alg = kv_tok * tok_bytes + B * hq * D * (ELEM + 4) + 4 * sum(len(t) for t in tables)
+    unique = (G * P0 + int(sum(cow[2])) + int(n_suf.sum()) + B) * tok_bytes
+    peak, pk = measured_peak()
+    emit({
+        "metric": "cfg3 prefix sharing: KV tokens/s (KV token-layers/s, append with "
+                  "copy-on-write + decode)",
+        "value": units / (ms / 1e3), "unit": "KV-token-layers/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random K/V/Q and tokens)",
+        "config": {"workload": f"cfg3: {B} requests in {G} groups sharing a {P0}-token prefix "
+                               f"(refcount {refcnt}) + partial tail (CoW), suffix U[128,512], "
+                               f"{L} layers", "q_heads": hq, "kv_heads": hk, "head_dim": D,
+                   "block_size": BS, "cow_per_layer": B},
+        "append_cow": {"kernel": "kv_append_vec_kernel", "avg_launch_ms": ams,
+                       "algorithmic_bytes_per_launch": app_alg,
+                       "gbs": app_alg / (ams / 1e3) / 1e9,
+                       "frac": app_alg / (ams / 1e3) / 1e9 / peak},
+        "roofline": {"bound": "hbm", "kernel": "paged_attn_mma_kernel", "avg_launch_ms": dms,
+                     "algorithmic_bytes_per_launch": dec_alg,
+                     "achieved": dec_alg / (dms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": dec_alg / (dms / 1e3) / 1e9 / peak, "peak_source": pk,
+                     "unique_kv_bytes_per_launch": unique,
+                     "note": "attended bytes; each shared prefix is attended by 64 "
+                             "requests, so most reads hit L2"},
+        "clocks": clocks})
 
 
 # ---------------------------------------------------------------------------
 # cfg5: continuous-batching churn, one shard of 1024 sequences per GPU
 # ---------------------------------------------------------------------------
 CFG5_SEQS, CFG5_SHARDS, CFG5_PREFIX = 1024, 8, 1024
+CFG5_MAX_MOVES = 512        # compaction moves per step (incremental packing)
 SRC_ROWS = 1 << 16          # random K/V source rows for prompt appends
 
 
@@ -1288,7 +1512,7 @@ def run_cfg5(args):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    layers = args.layers
+    layers = args.layers or 32
     ctx_all = lognormal_ctx(CFG5_SEQS, seed=args.seed + 5)
     shards = partition_by_context(ctx_all, CFG5_SHARDS)
     share = shards[rank]
@@ -1347,9 +1571,9 @@ def run_cfg5(args):
             if rng.random() < 0.5:
                 j = int(rng.integers(0, 4))
                 extra = max(1, c - CFG5_PREFIX)
-                out_p.append(pref[j] + [int(x) for x in rng.integers(0, 50000, size=extra)])
+                out_p.append(pref[j] + rng.integers(0, 50000, size=extra).tolist())
             else:
-                out_p.append([int(x) for x in rng.integers(0, 50000, size=c)])
+                out_p.append(rng.integers(0, 50000, size=c).tolist())
         return out_p
 
     # four popular prefixes, written once and published (owned by the tree)
@@ -1376,7 +1600,7 @@ def run_cfg5(args):
         e0 = torch.cuda.Event(enable_timing=True) if timed else None
         if e0 is not None:
             e0.record(stream)
-        moved = eng.compact()
+        moved = eng.compact(CFG5_MAX_MOVES)
         if e0 is not None and moved:
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record(stream)
@@ -1465,6 +1689,8 @@ def run_cfg5(args):
                                    "1024-token radix hit), LRU evict, compaction, decode",
                        "layers": layers, "q_heads": HQ, "kv_heads": HK, "head_dim": D,
                        "block_size": BS, "kv_dtype": "bf16", "seqs_per_rank": n_live,
+                       "compaction_moves_per_step_max": CFG5_MAX_MOVES,
+                       "pool_blocks_per_rank": n_blocks,
                        "parallelism": f"sequence-sharded x{world} (own pool + radix subtree)",
                        "l2": "every decode launch reads > 126 MB of KV"},
             "per_step": {"finished": stats["finished"] / steps,
@@ -1490,6 +1716,39 @@ def run_cfg5(args):
         dist.destroy_process_group()
 
 
+SECONDARY = (("cfg4", run_verify), ("prefill", run_prefill), ("prefill-d64", run_prefill),
+             ("append", run_append), ("copy", run_copy), ("cfg1", run_cfg1),
+             ("cfg2-f32", run_f32_decode), ("cfg3", run_cfg3))
+
+
+def run_secondary(args):
+    """The other configurations' lines, measured in the default run after the
+    headline's pool is released (5 timed steps after 3 warm-up each, own
+    clocks); a mode that fails records its error instead of a line."""
+    import copy
+
+    import torch
+    global _SINK
+    out = {}
+    for name, fn in SECONDARY:
+        a = copy.copy(args)
+        a.config, a.steps, a.warmup, a.gamma, a.no_cpu_baseline = name, 5, 3, 0, True
+        torch.cuda.empty_cache()
+        _SINK = []
+        t0 = time.perf_counter()
+        try:
+            fn(a)
+            lines = _SINK
+        except Exception as e:  # noqa: BLE001 - recorded, the headline still prints
+            lines = [{"error": f"{type(e).__name__}: {e}"}]
+        finally:
+            _SINK = None
+        for i, ln in enumerate(lines):
+            ln["wall_s"] = round(time.perf_counter() - t0, 1)
+            out[name if len(lines) == 1 else f"{name}#{i}"] = ln
+    return out
+
+
 def main():
     args = parse()
     if args.warmup < 3:
@@ -1510,8 +1769,14 @@ def main():
         run_f32_decode(args)
     elif args.config == "cfg5":
         run_cfg5(args)
+    elif args.config == "cfg3":
+        run_cfg3(args)
     else:
-        run_ours(args)
+        line = run_ours(args)
+        if line is not None:
+            if not args.no_secondary:
+                line["secondary"] = run_secondary(args)
+            print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -121,7 +121,12 @@ template <typename H> struct Vec8Half {
 template <> struct Vec8<__nv_bfloat16> : Vec8Half<__nv_bfloat16> {};
 template <> struct Vec8<__half> : Vec8Half<__half> {};
 
-// Vector form of the token rows of kv_append_kernel (no copy-on-write jobs).
+// Vector form of kv_append_kernel.  Copy-on-write jobs (the first nv slots
+// of block cow_src[c] into block cow_dst[c], every head, K and V) run first,
+// one warp per (job, head, K|V) region as 16-byte words; they touch slots
+// [0, nv) of the destination block, and every token slot the same launch
+// writes into that block is >= nv (checked on the host by the callers that
+// build the slots), so the two never overlap.
 // A CTA walks tokens t = blockIdx.x, blockIdx.x + gridDim.x, ...; its threads
 // own fixed 8-element chunks of a token's rows (ordered head, K|V, chunk, so
 // a warp writes whole contiguous rows), and each thread keeps kUnroll tokens'
@@ -132,12 +137,34 @@ template <typename S, typename P>
 __global__ void __launch_bounds__(256) kv_append_vec_kernel(
     P* __restrict__ kp, P* __restrict__ vp, PoolGeom g, int64_t layer,
     const S* __restrict__ kn, const S* __restrict__ vn, const int64_t* __restrict__ slots,
-    int64_t n_tok) {
+    int64_t n_tok, const int32_t* __restrict__ cow_src, const int32_t* __restrict__ cow_dst,
+    const int32_t* __restrict__ cow_nv, int64_t n_cow) {
     // same element type: move raw 16-byte words (no conversion, fewer
     // registers, more tokens in flight); otherwise convert through float
     constexpr bool kRaw = std::is_same<S, P>::value && sizeof(S) == 2;
     constexpr int kUnroll = kRaw ? 8 : 4;
     const int H = (int)g.n_kv_heads, D = (int)g.head_dim;
+    if (n_cow > 0) {
+        const int lane = threadIdx.x & 31;
+        const int64_t wpb = blockDim.x >> 5;
+        const int64_t regions = n_cow * H * 2;
+        for (int64_t j = blockIdx.x * wpb + (threadIdx.x >> 5); j < regions;
+             j += (int64_t)gridDim.x * wpb) {
+            const int64_t c = j / (2 * H);
+            const int h = (int)((j >> 1) % H);
+            const int64_t sb = cow_src[c], db = cow_dst[c], nv = cow_nv[c];
+            if (sb < 0 || sb >= g.n_blocks || db < 0 || db >= g.n_blocks || nv < 0 ||
+                nv > g.block_size) {
+                if (lane == 0) raise_flag(CX_DEV_BAD_BLOCK);
+                continue;
+            }
+            P* base = (j & 1) ? vp : kp;
+            const uint4* sw = reinterpret_cast<const uint4*>(base + g.tile(layer, sb, h));
+            uint4* dw = reinterpret_cast<uint4*>(base + g.tile(layer, db, h));
+            const int words = (int)(nv * D * (int64_t)sizeof(P) / 16);
+            for (int w = lane; w < words; w += 32) dw[w] = sw[w];
+        }
+    }
     const int cpr = D / 8;                              // chunks per row
     const int per_tok = H * 2 * cpr;
     const uint32_t bs = (uint32_t)g.block_size;
@@ -558,14 +585,15 @@ static void launch_append(const cx_pool* p, int64_t layer, const void* k, const 
                           const int32_t* cd, const int32_t* cn, int64_t n_cow, cudaStream_t st) {
     const uintptr_t al = reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
                          reinterpret_cast<uintptr_t>(p->k) | reinterpret_cast<uintptr_t>(p->v);
-    if (n_cow == 0 && p->head_dim % 8 == 0 && (al & 15) == 0 &&
-        p->n_blocks * p->block_size < (1ll << 31) &&
+    if (p->head_dim % 8 == 0 && (al & 15) == 0 && p->n_blocks * p->block_size < (1ll << 31) &&
         p->n_kv_heads * 2 * (p->head_dim / 8) <= (1 << 20)) {
-        int64_t blocks = n_tok < (int64_t)num_sms() * 16 ? n_tok : (int64_t)num_sms() * 16;
+        const int64_t cap = (int64_t)num_sms() * 16;
+        int64_t blocks = n_tok > n_cow * p->n_kv_heads / 4 ? n_tok : n_cow * p->n_kv_heads / 4;
+        blocks = blocks < cap ? blocks : cap;
         if (blocks < 1) blocks = 1;
         kv_append_vec_kernel<S, P><<<(unsigned)blocks, 256, 0, st>>>(
             static_cast<P*>(p->k), static_cast<P*>(p->v), geom_of(p), layer,
-            static_cast<const S*>(k), static_cast<const S*>(v), slots, n_tok);
+            static_cast<const S*>(k), static_cast<const S*>(v), slots, n_tok, cs, cd, cn, n_cow);
         return;
     }
     const int64_t jobs = (n_tok + n_cow) * p->n_kv_heads;

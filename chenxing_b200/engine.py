@@ -90,6 +90,7 @@ class BatchedKVEngine:
         self.free_private_blocks = free_private_blocks
         self.seqs: dict = {}
         self._alias_refs: Counter = Counter()     # block id -> live sequences aliasing it
+        self._held: Counter = Counter()           # block id -> live tables listing it
 
     # ------------------------------------------------------------------ #
     # admission / lifecycle
@@ -133,6 +134,7 @@ class BatchedKVEngine:
         if s.n_tokens == len(s.tokens):
             s.n_tokens -= 1
         self.seqs[seq_id] = s
+        self._held.update(s.block_table)
         return s
 
     def finish(self, seq_id: int, publish: bool = True) -> None:
@@ -155,11 +157,11 @@ class BatchedKVEngine:
             self._alias_refs[b] -= 1
             if self._alias_refs[b] <= 0:
                 del self._alias_refs[b]
+        self._unhold(s.block_table)
         if self.free_private_blocks:
-            owned = self._tree_blocks()
-            held = {b for o in self.seqs.values() for b in o.block_table}
+            # blocks no radix node and no other live table lists
             for b in s.block_table:
-                if b not in owned and b not in held:
+                if not c.tree_holds(b) and b not in self._held:
                     c._free_block(b)
 
     def publish(self, seq_id: int) -> bool:
@@ -197,13 +199,11 @@ class BatchedKVEngine:
         """Append generated / drafted token ids (Sequence.generated)."""
         self.seqs[seq_id].tokens.extend(int(t) for t in new_tokens)
 
-    def _tree_blocks(self) -> set:
-        out, stack = set(), [self.cache._root]
-        while stack:
-            n = stack.pop()
-            out.update(n.blocks)
-            stack.extend(n.children.values())
-        return out
+    def _unhold(self, blocks) -> None:
+        self._held.subtract(blocks)
+        for b in blocks:
+            if self._held[b] <= 0:
+                del self._held[b]
 
     # ------------------------------------------------------------------ #
     # one step
@@ -259,6 +259,8 @@ class BatchedKVEngine:
                         dst = c.alloc_block()
                         cow.append((src, dst, s.n_tokens - j * bs if j == first else 0))
                         s.block_table[j] = dst
+                        self._unhold([src])
+                        self._held[dst] += 1
                     self._alias_refs[src] -= 1
                     if self._alias_refs[src] <= 0:
                         del self._alias_refs[src]
@@ -269,7 +271,9 @@ class BatchedKVEngine:
                 need = -(-(target - have) // bs)
                 c.ensure_free(need)
                 for _ in range(need):
-                    s.block_table.append(c.alloc_block())
+                    b = c.alloc_block()
+                    s.block_table.append(b)
+                    self._held[b] += 1
         return StepPlan(seqs, n_past, ql, None, None, None, cow)
 
     def append(self, plan: StepPlan, layer: int, k, v) -> None:
@@ -323,10 +327,13 @@ class BatchedKVEngine:
         radix tree are relabelled, the K/V moved by one block-copy launch);
         returns blocks moved."""
         live = [s.block_table for s in self.seqs.values()]
-        if isinstance(self.cache, RadixPagedKVCache):
-            n = self.cache.compact(live, max_moves)
-        else:                                   # bare RadixIndex: metadata only
-            n = len(self.cache.plan_compaction(live, max_moves)[0])
+        src, dst = self.cache.plan_compaction(live, max_moves)
+        if src and isinstance(self.cache, RadixPagedKVCache):
+            self.cache.copy_blocks(src, dst)     # bare RadixIndex: metadata only
+        n = len(src)
+        for a, b in zip(src, dst):
+            if a in self._held:
+                self._held[b] += self._held.pop(a)
         if n and self._alias_refs:
             refs = Counter()
             for s in self.seqs.values():

@@ -24,6 +24,7 @@ n_kv_heads, head_dim)`` as a strided view of that storage.
 from __future__ import annotations
 
 import time
+from collections import Counter
 from dataclasses import dataclass
 
 import numpy as np
@@ -85,6 +86,9 @@ class RadixIndex:
         self._root = _RadixNode([], [], None, self._clock())
         self._hits = 0
         self._lookups = 0
+        # block id -> references from nodes reachable from the root, kept by
+        # insert / evict / plan_compaction (what a walk of the tree would give)
+        self._owned: Counter = Counter()
 
     @property
     def free_blocks(self) -> int:
@@ -149,11 +153,31 @@ class RadixIndex:
         if parent.is_leaf and parent.refcnt == 0 and parent is not self._root:
             parent.tokens.extend(token_ids)
             parent.blocks.extend(block_ids)
+            self._owned.update(block_ids)
             self._touch(parent)
             return parent
         child = _RadixNode(list(token_ids), list(block_ids), parent, self._clock())
+        old = parent.children.get(token_ids[0])
         parent.children[token_ids[0]] = child
+        if old is not None:                   # a replaced sibling drops out of the tree
+            self._disown(old)
+        self._owned.update(block_ids)
         return child
+
+    def _disown(self, node: _RadixNode) -> None:
+        """``node`` and its subtree left the tree: drop their block references."""
+        stack = [node]
+        while stack:
+            n = stack.pop()
+            self._owned.subtract(n.blocks)
+            for b in n.blocks:
+                if self._owned[b] <= 0:
+                    del self._owned[b]
+            stack.extend(n.children.values())
+
+    def tree_holds(self, block_id: int) -> bool:
+        """Whether a node reachable from the root lists ``block_id``."""
+        return block_id in self._owned
 
     def acquire(self, node: _RadixNode) -> None:
         """Pin ``node`` and its ancestors (radix_kv.py:205-211)."""
@@ -183,6 +207,7 @@ class RadixIndex:
             for b in victim.blocks:
                 self._free_block(b)
             del victim.parent.children[victim.tokens[0]]
+            self._disown(victim)
         return freed
 
     def ensure_free(self, n_needed: int) -> None:
@@ -237,6 +262,9 @@ class RadixIndex:
             stack.extend(node.children.values())
         for t in tables:
             t[:] = [remap.get(b, b) for b in t]
+        for a, b in remap.items():
+            if a in self._owned:
+                self._owned[b] += self._owned.pop(a)
         for d in dst:
             del self._free[d]
         for s in sorted(src):
@@ -252,6 +280,25 @@ class RadixIndex:
         return {"n_blocks": self.n_blocks, "free_blocks": self.free_blocks,
                 "cached_blocks": self.n_blocks - self.free_blocks, "radix_nodes": total,
                 "prefix_hit_rate": self._hits / max(self._lookups, 1)}
+
+
+def _check_cow_slots(slots, cow, block_size: int) -> None:
+    """Raise ValueError if a slot lands inside the copied prefix of a
+    copy-on-write destination block (the copy and the stores of one append
+    launch run concurrently).  Device tensors are not inspected: reading them
+    would synchronise the stream."""
+    if any(isinstance(x, torch.Tensor) and x.is_cuda for x in (slots, *cow)):
+        return
+    s = np.asarray(slots.numpy() if isinstance(slots, torch.Tensor) else slots,
+                   dtype=np.int64).reshape(-1)
+    _, dst, nv = (np.asarray(c.numpy() if isinstance(c, torch.Tensor) else c,
+                             dtype=np.int64).reshape(-1) for c in cow)
+    live = s[s >= 0]
+    blk, off = live // block_size, live % block_size
+    for d, n in zip(dst, nv):
+        if np.any((blk == d) & (off < n)):
+            raise ValueError(f"copy-on-write: a slot of block {int(d)} falls inside its "
+                             f"{int(n)} copied rows")
 
 
 class RadixPagedKVCache(RadixIndex):
@@ -429,7 +476,12 @@ class RadixPagedKVCache(RadixIndex):
     def append_batch(self, layer: int, k, v, slot_mapping, cow=None) -> None:
         """k, v: (T, H, D) rows for T tokens of many sequences; slot_mapping:
         (T,) physical slots (``batch.slot_mapping``); optional copy-on-write
-        triple (src, dst, n_valid) applied to this layer first."""
+        triple (src, dst, n_valid): the first n_valid slots of block src are
+        copied into block dst for this layer in the same launch, so no slot
+        of the call may fall inside them (checked here for host arrays;
+        ``BatchedKVEngine`` builds its slots that way)."""
+        if cow is not None:
+            _check_cow_slots(slot_mapping, cow, self.block_size)
         kt = to_device(k, self.device)
         vt = to_device(v, self.device)
         st = to_device(slot_mapping, self.device, float_only=False).to(torch.int64)

@@ -95,11 +95,14 @@ int cx_device_error(void* stream, int clear, uint32_t* flags);
  * Token t (k_new/v_new row t, shape [n_tokens][n_kv_heads][head_dim] of
  * src_dtype) is stored at slot slot_mapping[t] = block*block_size + offset of
  * `layer`; a negative slot skips the token.  Values are rounded to the pool
- * type with round-to-nearest-even.  Before the scatter, for c < n_cow the
+ * type with round-to-nearest-even.  In the same launch, for c < n_cow the
  * first cow_n_valid[c] slots of block cow_src[c] are copied into block
  * cow_dst[c] for this layer (copy-on-write of a shared partial tail block; the
  * reference has no counterpart, it shares whole blocks only, radix_kv.py:16-21).
- * cow_* may be NULL when n_cow == 0. */
+ * The copies and the token stores run concurrently: every slot the call
+ * writes in a block cow_dst[c] must be at offset >= cow_n_valid[c] (the
+ * Python layer checks this before the launch).  cow_* may be NULL when
+ * n_cow == 0. */
 int cx_kv_append(const cx_pool* pool, int64_t layer,
                  const void* k_new, const void* v_new, int32_t src_dtype,
                  const int64_t* slot_mapping, int64_t n_tokens,

@@ -23,10 +23,18 @@ Writes:
   rope.npz        reference build_rope_cache tables (plain and YaRN-scaled) and
                   apply_rope outputs (half-split and interleaved layouts, token
                   positions picked from the table) on seeded inputs.
+  tiny_model.npz  the reference's own tiny seeded target and draft models
+                  (tests/conftest.py of the reference) run through its
+                  LLMEngine and SpeculativeDecoder: their weights, the logits
+                  of the full / incremental / rollback-and-rewrite prefills of
+                  its tests/test_transformer.py:7-23, and the greedy target
+                  and speculative (gamma 1, 2, 4, 8) outputs of its
+                  tests/test_speculative.py:14-21.
 
     python tests/golden/make_golden.py --reference <path> --only rope
+    python tests/golden/make_golden.py --reference <path> --only model
 
-regenerates rope.npz alone.
+regenerate rope.npz / tiny_model.npz alone.
 """
 from __future__ import annotations
 
@@ -309,11 +317,80 @@ def rope_goldens(build_rope_cache, apply_rope, seed=21):
     return out
 
 
+def model_goldens(ModelConfig, build_tiny_model, LLMEngine, SamplingParams,
+                  SpeculativeDecoder):
+    """Reference tiny models (vocab 264, hidden 64, intermediate 128, 2 layers,
+    4 query / 2 KV heads, head_dim 16; draft = that config scaled by 0.5,
+    seeds 42 and 99, block size 8, 64 blocks) and the prompt of the
+    reference's conftest (10 tokens from default_rng(1))."""
+    cfg = ModelConfig(vocab_size=264, hidden_size=64, intermediate_size=128,
+                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2)
+    target, tw = build_tiny_model(cfg, seed=42)
+    dcfg = cfg.scaled(0.5)
+    draft, dw = build_tiny_model(dcfg, seed=99)
+    prompt = list(map(int, np.random.default_rng(1).integers(0, 256, 10)))
+
+    def engine(m):
+        return LLMEngine(m, None, block_size=8, n_blocks=64)
+
+    out = {"prompt": np.asarray(prompt, dtype=np.int64)}
+    for tag, c in (("t", cfg), ("d", dcfg)):
+        out[f"{tag}.config"] = np.asarray(
+            [c.vocab_size, c.hidden_size, c.intermediate_size, c.num_hidden_layers,
+             c.num_attention_heads, c.num_key_value_heads, c.head_dim], dtype=np.int64)
+        out[f"{tag}.rope"] = np.asarray([c.rope_theta, c.rms_norm_eps,
+                                         c.max_position_embeddings], dtype=np.float64)
+    for tag, w in (("t", tw), ("d", dw)):
+        for k, v in w.items():
+            out[f"{tag}.{k}"] = np.asarray(v, dtype=np.float32)
+    e = engine(target)
+    seq = e.create_sequence(prompt, SamplingParams(max_tokens=1))
+    out["logits_full"] = e.prefill(seq).copy()
+    e = engine(target)
+    seq = e.create_sequence(prompt[:7], SamplingParams(max_tokens=1))
+    e.prefill(seq)
+    out["logits_incremental"] = e.forward_ids(seq, prompt[7:], allow_unconfirmed=True)
+    e = engine(target)
+    seq = e.create_sequence(prompt, SamplingParams(max_tokens=1))
+    e.prefill(seq)
+    seq.n_tokens = 5
+    out["logits_rewrite"] = e.forward_ids(seq, prompt[5:], allow_unconfirmed=True)
+    greedy = SamplingParams(max_tokens=16, temperature=0.0, seed=7)
+    toks, _ = engine(target).generate(prompt, greedy)
+    out["greedy_tokens"] = np.asarray(toks, dtype=np.int64)
+    # teacher-forced logits over prompt + greedy tokens: the argmax margins
+    e = engine(target)
+    seq = e.create_sequence(prompt + toks, SamplingParams(max_tokens=1))
+    seq.block_table = []
+    seq.n_tokens = 0
+    out["logits_teacher"] = e.forward_ids(seq, prompt + toks)
+    for gamma in (1, 2, 4, 8):
+        sd = SpeculativeDecoder(engine(target), engine(draft), num_speculative_tokens=gamma)
+        o, _ = sd.generate(prompt, greedy)
+        out[f"spec_tokens_{gamma}"] = np.asarray(o, dtype=np.int64)
+        out[f"spec_stats_{gamma}"] = np.asarray([sd.stats.steps, sd.stats.drafted,
+                                                sd.stats.accepted], dtype=np.int64)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to a Chenxing checkout")
-    ap.add_argument("--only", choices=["rope"], default=None)
+    ap.add_argument("--only", choices=["rope", "model"], default=None)
     args = ap.parse_args()
+    if args.only == "model" or args.only is None:
+        sys.path.insert(0, args.reference)
+        from chenxing.core.sampler import SamplingParams
+        from chenxing.engine.engine import LLMEngine
+        from chenxing.engine.speculative import SpeculativeDecoder
+        from chenxing.model.config import ModelConfig
+        from chenxing.model.transformer import build_tiny_model
+        np.savez_compressed(os.path.join(HERE, "tiny_model.npz"),
+                            **model_goldens(ModelConfig, build_tiny_model, LLMEngine,
+                                            SamplingParams, SpeculativeDecoder))
+        print("tiny_model.npz written to", HERE)
+        if args.only == "model":
+            return
     if args.only == "rope":
         sys.path.insert(0, args.reference)
         from chenxing.core.tensor import apply_rope, build_rope_cache

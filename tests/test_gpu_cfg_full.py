@@ -255,7 +255,8 @@ def test_cfg3_full_size_prefix_share_cow_decode():
 # ---------------------------------------------------------------------------
 # cfg5: continuous-batching churn on one rank's share, through the engine
 # ---------------------------------------------------------------------------
-def test_cfg5_rank_share_churn_evict_compact_decode():
+@pytest.mark.parametrize("publish_mode", ["suffix", "reference"])
+def test_cfg5_rank_share_churn_evict_compact_decode(publish_mode):
     """One rank's share (partition_by_context over 8 ranks) of 1024 sequences
     with lognormal contexts (median 2048, sigma 1.0, cap 32768), Hq 32 /
     Hkv 8, D 128, bf16.  Per step: 5 % finish (prefix published, private
@@ -263,7 +264,16 @@ def test_cfg5_rank_share_churn_evict_compact_decode():
     radix hit, LRU eviction plus compaction, then one batched decode step.
     Metadata is compared with the oracle engine replay after every step;
     pool contents with a device-side shadow of every sequence's K/V
-    (bit-exact); decode rows of sampled sequences with the oracle."""
+    (bit-exact); decode rows of sampled sequences with the oracle.
+
+    ``publish_mode="reference"`` publishes as the reference does (the whole
+    chain from token 0 under the hit node).  Evicting such a node frees blocks
+    that live sequences still use; at this size and seed no eviction does so,
+    which the test asserts before trusting the pool comparison.  In that
+    mode the finishing sequences are drawn from those admitted without a radix
+    hit: a finished hit sequence's duplicate chain would be the first LRU
+    victim and free its hit prefix under the live sequences (the reference
+    hazard, shown on the host by test_host_cpu)."""
     from chenxing_b200 import RadixPagedKVCache
     from chenxing_b200.engine import BatchedKVEngine
     from chenxing_b200.sharding import partition_by_context
@@ -283,8 +293,9 @@ def test_cfg5_rank_share_churn_evict_compact_decode():
     meta = OraclePagedKVCache(n_blocks, BS, 1, HK, D, with_pool=False, clock=clock_b)
     # suffix publication: the reference's whole-chain publication under the
     # hit node lets eviction free blocks still pinned by live sequences
-    eng = BatchedKVEngine(cache, n_q_heads=HQ, free_private_blocks=True, publish_mode="suffix")
-    ref = OracleEngine(meta, free_private=True, suffix_publish=True)
+    eng = BatchedKVEngine(cache, n_q_heads=HQ, free_private_blocks=True,
+                          publish_mode=publish_mode)
+    ref = OracleEngine(meta, free_private=True, suffix_publish=publish_mode == "suffix")
     g = torch.Generator(device="cuda")
     g.manual_seed(5)
     shadow = {}
@@ -350,15 +361,21 @@ def test_cfg5_rank_share_churn_evict_compact_decode():
     moved_total = 0
     for step in range(3):
         live = sorted(eng.seqs)
-        done = [live[i] for i in rng.choice(len(live), size=max(1, len(live) // 20),
-                                            replace=False)]
+        pool_ids = live if publish_mode == "suffix" else \
+            [sid for sid in live if eng.seqs[sid].radix_node is None]
+        done = [pool_ids[i] for i in rng.choice(len(pool_ids), size=max(1, len(live) // 20),
+                                                replace=False)]
         for sid in done:
             eng.finish(sid)
             ref.finish(sid)
             shadow.pop(sid)
         admit([next(new_ctx) for _ in done])
         k_ev = int(rng.integers(16, 256))
+        live_blocks = {b for s in eng.seqs.values() for b in s.block_table}
+        free_before = set(cache._free)
         assert cache.evict(k_ev) == meta.evict(k_ev)
+        freed = set(cache._free) - free_before
+        assert not freed & live_blocks, "eviction freed blocks of live sequences"
         moved = eng.compact()
         assert moved == len(ref.compact())
         moved_total += moved

@@ -500,6 +500,42 @@ def test_fused_cow_in_append_bit_exact():
     assert not c.k_pool[1, 4, 8:].any() and not c.k_pool[0, 4].any()
 
 
+@pytest.mark.parametrize("dtype,d", [("bfloat16", 128), (np.float32, 64), ("bfloat16", 40)],
+                         ids=["bf16-d128-vector", "f32-d64-vector", "bf16-d40-scalar"])
+def test_fused_cow_many_jobs_with_token_stores_bit_exact(dtype, d):
+    """Ten copy-on-write jobs (1-15 valid rows each) in one append launch with
+    token stores behind the copied rows of the same blocks and into other
+    blocks: the vector kernel (16-byte rows) and the element-wise kernel give
+    exactly the copy followed by the stores, on the target layer only."""
+    from chenxing_b200 import RadixPagedKVCache
+    rng = np.random.default_rng(9)
+    H, L = 4, 2
+    c = RadixPagedKVCache(40, 16, L, H, d, dtype=dtype, host_io=False)
+    for layer in range(L):
+        kv = rng.standard_normal((20 * 16, H, d)).astype(np.float32)
+        c.write_layer(list(range(20)), 0, layer, kv, kv * 0.5)
+    src, dst = np.arange(10), np.arange(20, 30)
+    nv = rng.integers(1, 16, size=10)
+    slots = [int(b) * 16 + int(o) for b, n in zip(dst, nv)
+             for o in range(int(n), min(16, int(n) + 3))]
+    slots += [30 * 16 + i for i in range(0, 160, 7)]
+    T = len(slots)
+    k = rng.standard_normal((T, H, d)).astype(np.float32)
+    v = rng.standard_normal((T, H, d)).astype(np.float32)
+    want_k, want_v = c._k.clone(), c._v.clone()
+    for a, b, n in zip(src, dst, nv):
+        want_k[1, b, :, :n] = want_k[1, a, :, :n]
+        want_v[1, b, :, :n] = want_v[1, a, :, :n]
+    kt = torch.from_numpy(k).to(c.torch_dtype).cuda()
+    vt = torch.from_numpy(v).to(c.torch_dtype).cuda()
+    for i, sl in enumerate(slots):
+        want_k[1, sl // 16, :, sl % 16] = kt[i]
+        want_v[1, sl // 16, :, sl % 16] = vt[i]
+    c.append_batch(1, k, v, np.array(slots), cow=(src, dst, nv))
+    torch.cuda.synchronize()
+    assert torch.equal(c._k, want_k) and torch.equal(c._v, want_v)
+
+
 # ---------------------------------------------------------------------------
 # device-side range checks: flagged, never faulting
 # ---------------------------------------------------------------------------

@@ -278,6 +278,15 @@ def test_batched_engine_metadata_matches_oracle_replay(free_private, mode):
             {k: (s["table"], s["n"]) for k, s in ref.seqs.items()}
         assert list(idx._free) == list(orc._free)
         assert tree_sig(idx._root) == tree_sig(orc._root)
+        # the incremental block counts equal a full walk of the tree / tables
+        from collections import Counter
+        walk, stack = Counter(), [idx._root]
+        while stack:
+            n = stack.pop()
+            walk.update(n.blocks)
+            stack.extend(n.children.values())
+        assert walk == idx._owned
+        assert Counter(b for s in eng.seqs.values() for b in s.block_table) == eng._held
 
     for _ in range(12):
         admit()
@@ -336,3 +345,15 @@ def test_reference_publish_lets_eviction_free_pinned_blocks(mode):
     freed = [b for b in pinned if b in idx._free]
     assert bool(freed) == (mode == "reference")
 
+
+
+def test_cow_slots_inside_the_copied_rows_are_rejected():
+    """An append's copy-on-write copies and its token stores run in one
+    launch, so no token may land inside a destination block's copied rows."""
+    from chenxing_b200.radix_kv import _check_cow_slots
+    cow = (np.array([3, 5]), np.array([4, 6]), np.array([7, 2]))
+    _check_cow_slots(np.array([4 * 16 + 7, 6 * 16 + 2, 9 * 16, -1]), cow, 16)
+    with pytest.raises(ValueError):
+        _check_cow_slots(np.array([4 * 16 + 6]), cow, 16)
+    with pytest.raises(ValueError):
+        _check_cow_slots([6 * 16 + 1, 4 * 16 + 8], cow, 16)
