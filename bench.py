@@ -59,7 +59,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["cfg2", "small", "prefill", "prefill-small",
                                          "prefill-d64", "append", "cfg4", "cfg4-small",
-                                         "copy", "cfg1", "cfg2-f32", "cfg5", "cfg3"],
+                                         "copy", "cfg1", "cfg2-f32", "cfg5", "cfg3",
+                                         "dense"],
                     default="cfg2",
                     help="small: 1 layer, pool sized to need (~2 GB, for profiler captures); "
                          "prefill: chunked-prefill attention on the tcgen05 kernel (its own "
@@ -1286,7 +1287,9 @@ def run_f32_decode(args):
     if _lib.device_flags(clear=True):
         raise RuntimeError("device flags raised during the fp32 decode bench")
     ms = start.elapsed_time(end) / args.steps
-    units = sum(int((ctx0 + args.warmup + i + 1).sum()) for i in range(args.steps)) * layers
+    # KV token-layers of one step (the mean over the timed steps), per ms_per_step
+    units = sum(int((ctx0 + args.warmup + i + 1).sum()) for i in range(args.steps)) * layers \
+        / args.steps
     dms = float(np.mean([a.elapsed_time(b) for a, b, _ in dec_ev]))
     kv_tok = float(np.mean([int((ctx0 + s + 1).sum()) for _, _, s in dec_ev]))
     nblk = sum(len(t) for t in wl.block_tables)
@@ -1307,6 +1310,90 @@ def run_f32_decode(args):
                      "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_source": pk,
                      "algorithmic_bytes_per_launch": alg, "avg_launch_ms": dms},
         "clocks": clocks})
+
+
+# ---------------------------------------------------------------------------
+# the generic kernel: dense flash_attention and an fp16 pool (separate mode)
+# ---------------------------------------------------------------------------
+def run_dense(args):
+    """Two HBM-bound shapes only the tiled generic kernel serves, each its own
+    line: (1) the dense flash_attention drop-in (cx_attention_dense) at a
+    decode shape, 64 sequences x Hq 32 / Hkv 8 x 4096 keys, D 128, fp32 K/V and
+    Q, causal; (2) the cfg2 decode shape on an fp16 pool (64 sequences, ctx ~
+    U[1024, 8192], blocks scattered).  Algorithmic bytes = K + V read once +
+    Q + fp32 output (+ block tables)."""
+    import torch
+    from chenxing_b200 import PagedBatch, RadixPagedKVCache, _lib
+    from chenxing_b200.workloads import cfg2_meta
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    peak, pk = measured_peak()
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed)
+
+    def timed(launch):
+        for _ in range(args.warmup):
+            launch()
+        torch.cuda.synchronize(dev)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        sampler = ClockSampler(device_uuid(dev))
+        sampler.start()
+        time.sleep(0.5)
+        for e0, e1 in evs:
+            e0.record(stream)
+            launch()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        clocks = sampler.stop()
+        if _lib.device_flags(clear=True):
+            raise RuntimeError("device flags raised during the dense bench")
+        return float(np.mean([a.elapsed_time(b) for a, b in evs])), clocks
+
+    def line(metric, alg, avg, clocks, workload):
+        gbs = alg / (avg / 1e3) / 1e9
+        emit({"metric": metric, "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+              "warmup": args.warmup, "ms_per_step": avg, "higher_is_better": True,
+              "scaling": "none", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+              "config": {"workload": workload, "kernel": "generic"},
+              "roofline": {"bound": "hbm", "kernel": "attn_generic_kernel", "achieved": gbs,
+                           "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_source": pk,
+                           "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg},
+              "clocks": clocks})
+
+    B, SK = 64, 4096
+    q = torch.randn((B, HQ, 1, D), device=dev, generator=g)
+    k = torch.randn((B, HK, SK, D), device=dev, generator=g)
+    v = torch.randn((B, HK, SK, D), device=dev, generator=g)
+    out = torch.empty((B, HQ, 1, D), dtype=torch.float32, device=dev)
+    avg, clocks = timed(lambda: _lib.check(lib.cx_attention_dense(
+        q.data_ptr(), _lib.CX_F32, k.data_ptr(), v.data_ptr(), _lib.CX_F32, B, HQ, 1, HK, SK, D,
+        D, 1, 0, None, float("nan"), out.data_ptr(), sp), "cx_attention_dense"))
+    alg = 2 * B * HK * SK * D * 4 + 2 * B * HQ * D * 4
+    line("dense flash_attention GB/s (cx_attention_dense, decode shape, fp32)", alg, avg, clocks,
+         f"{B} seqs x {SK} keys, Hq {HQ} / Hkv {HK}, D {D}, fp32, causal")
+    del q, k, v, out
+    torch.cuda.empty_cache()
+
+    n_blocks = BATCH * (-(-(8192 + 1) // BS)) + 64
+    wl = cfg2_meta(n_blocks=n_blocks, seed=args.seed, batch=BATCH, n_layers=1)
+    cache = RadixPagedKVCache(n_blocks, BS, 1, HK, D, dtype="float16", device=dev,
+                              host_io=False)
+    cache._k.normal_(0.0, 1.0 / math.sqrt(D), generator=g)
+    cache._v.normal_(0.0, 1.0 / math.sqrt(D), generator=g)
+    batch = PagedBatch(cache, wl.block_tables, wl.ctx_lens, n_q_heads=HQ)
+    qh = (torch.randn((BATCH, HQ, D), device=dev, generator=g) / math.sqrt(D)).half()
+    o2 = torch.empty((BATCH, HQ, D), dtype=torch.float32, device=dev)
+    assert batch.kernel_kind(qh.dtype) == "generic"
+    avg, clocks = timed(lambda: cache.decode_batch(0, qh, batch, o2))
+    alg = int(wl.ctx_lens.sum()) * 2 * HK * D * 2 + BATCH * HQ * D * (2 + 4) + \
+        4 * sum(len(t) for t in wl.block_tables)
+    line("paged decode GB/s on an fp16 pool (generic kernel, cfg2 shape)", alg, avg, clocks,
+         f"{BATCH} seqs, ctx U[1024,8192], Hq {HQ} / Hkv {HK}, D {D}, fp16 pool")
 
 
 # ---------------------------------------------------------------------------
@@ -1597,14 +1684,11 @@ def run_cfg5(args):
         prefill(prompts_for([next(new_ctx) for _ in range(n_fin)]))
         stats["finished"] += n_fin
         stats["evicted"] += cache.evict(int(rng.integers(16, 256)))
-        e0 = torch.cuda.Event(enable_timing=True) if timed else None
-        if e0 is not None:
-            e0.record(stream)
-        moved = eng.compact(CFG5_MAX_MOVES)
-        if e0 is not None and moved:
-            e1 = torch.cuda.Event(enable_timing=True)
-            e1.record(stream)
-            copy_ev.append((e0, e1, moved))
+        evs = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) \
+            if timed else None
+        moved = eng.compact(CFG5_MAX_MOVES, events=evs)
+        if evs is not None and moved:
+            copy_ev.append((evs[0], evs[1], moved))
         stats["moved"] += moved
         ids = sorted(eng.seqs)
         p = eng.plan(ids)
@@ -1718,7 +1802,7 @@ def run_cfg5(args):
 
 SECONDARY = (("cfg4", run_verify), ("prefill", run_prefill), ("prefill-d64", run_prefill),
              ("append", run_append), ("copy", run_copy), ("cfg1", run_cfg1),
-             ("cfg2-f32", run_f32_decode), ("cfg3", run_cfg3))
+             ("cfg2-f32", run_f32_decode), ("cfg3", run_cfg3), ("dense", run_dense))
 
 
 def run_secondary(args):
@@ -1771,6 +1855,8 @@ def main():
         run_cfg5(args)
     elif args.config == "cfg3":
         run_cfg3(args)
+    elif args.config == "dense":
+        run_dense(args)
     else:
         line = run_ours(args)
         if line is not None:

@@ -959,13 +959,22 @@ static int launch_f32_cfg(const CUtensorMap& tk, const CUtensorMap& tv, MmaParam
     using C = F32Cfg<D, HG, RT>;
     auto kern = paged_attn_f32_kernel<D, HG, RT>;
     // key slices: the ring length must be a multiple of them (each stage is
-    // always consumed by the same slice); take the longest ring, and on a tie
-    // the most consumer warps
+    // always consumed by the same slice).  Take the most consumer warps whose
+    // ring still holds at least 4 stages and 3/4 of the longest ring: one warp
+    // per head walks its units serially (a 4-unit chunk at 1 slice measured
+    // 33 us for cfg1, the SMs busy 14 % of it), while a ring shortened from 6
+    // to 4 stages of 32 KB costs more than the third and fourth slice give.
     const int max_ks = C::MAX_CONSUMERS / (HG * p.mt);
+    int stg_of[kConsumerWarps + 1] = {};
+    int longest = 0;
+    for (int ks = 1; ks <= max_ks; ++ks) {
+        stg_of[ks] = (C::raw_stages(p.rows, p.mt, ks) / ks) * ks;
+        longest = stg_of[ks] > longest ? stg_of[ks] : longest;
+    }
     int best_ks = 0, best_st = 0;
     for (int ks = 1; ks <= max_ks; ++ks) {
-        const int stg = (C::raw_stages(p.rows, p.mt, ks) / ks) * ks;
-        if (stg >= 2 && stg >= best_st) {
+        const int stg = stg_of[ks];
+        if (stg >= 2 && (best_ks == 0 || (stg >= 4 && 4 * stg >= 3 * longest))) {
             best_st = stg;
             best_ks = ks;
         }

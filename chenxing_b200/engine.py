@@ -322,14 +322,15 @@ class BatchedKVEngine:
             s.n_tokens += int(n)
 
     # ------------------------------------------------------------------ #
-    def compact(self, max_moves: int | None = None) -> int:
+    def compact(self, max_moves: int | None = None, events=None) -> int:
         """Pack in-use blocks into the lowest ids (every live table and the
         radix tree are relabelled, the K/V moved by one block-copy launch);
-        returns blocks moved."""
+        returns blocks moved.  ``events``: optional pair of CUDA events
+        recorded around the copy launch (when there is one)."""
         live = [s.block_table for s in self.seqs.values()]
         src, dst = self.cache.plan_compaction(live, max_moves)
         if src and isinstance(self.cache, RadixPagedKVCache):
-            self.cache.copy_blocks(src, dst)     # bare RadixIndex: metadata only
+            self.cache.copy_blocks(src, dst, events=events)   # bare RadixIndex: metadata only
         n = len(src)
         for a, b in zip(src, dst):
             if a in self._held:

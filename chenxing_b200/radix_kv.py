@@ -245,7 +245,7 @@ class RadixIndex:
         Every live block table must be passed, or it keeps stale ids.
         """
         n_used = self.n_blocks - len(self._free)
-        holes = [b for b in range(n_used) if b in self._free]
+        holes = sorted(b for b in self._free if b < n_used)
         high = [b for b in range(self.n_blocks - 1, n_used - 1, -1) if b not in self._free]
         n = min(len(holes), len(high))
         if max_moves is not None:
@@ -423,9 +423,11 @@ class RadixPagedKVCache(RadixIndex):
             return to_numpy(ko), to_numpy(vo)
         return ko, vo
 
-    def copy_blocks(self, src: list, dst: list, n_slots: int | None = None) -> None:
+    def copy_blocks(self, src: list, dst: list, n_slots: int | None = None,
+                    events=None) -> None:
         """Copy slots [0, n_slots) of block src[i] into block dst[i], every layer,
-        K and V (eviction compaction / prefix forking)."""
+        K and V (eviction compaction / prefix forking).  ``events``: an optional
+        pair of CUDA events recorded right before and after the copy launch."""
         if len(src) != len(dst):
             raise ValueError("src and dst must have the same length")
         if not src:
@@ -437,9 +439,13 @@ class RadixPagedKVCache(RadixIndex):
         n_slots = self.block_size if n_slots is None else int(n_slots)
         s = upload(np.asarray(src, dtype=np.int32), self.device)
         t = upload(np.asarray(dst, dtype=np.int32), self.device)
+        if events is not None:
+            events[0].record()
         _lib.check(_lib.lib().cx_block_copy(self._pool, s.data_ptr(), t.data_ptr(), len(src),
                                             n_slots, _lib.stream_ptr(self.device)),
                    "cx_block_copy")
+        if events is not None:
+            events[1].record()
 
     def compact(self, tables=(), max_moves: int | None = None) -> int:
         """Pack in-use blocks into the lowest ids (``plan_compaction``) and move

@@ -52,6 +52,9 @@ class PagedCase:
             self.cache.append_batch(layer, k, v, slots)
         if dtype == "bfloat16":
             k, v = bf16_round(k), bf16_round(v)
+        elif dtype == "float16":            # round-to-nearest-even, as the pool stores
+            k = k.astype(np.float16).astype(np.float32)
+            v = v.astype(np.float16).astype(np.float32)
         self.k, self.v = k, v
         self.q = (rng.standard_normal((int(self.q_lens.sum()), hq, d)) * q_scale).astype(np.float32)
         self.q_dev = torch.from_numpy(self.q).to(q_dtype).cuda()

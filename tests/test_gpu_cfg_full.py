@@ -90,7 +90,8 @@ def test_cfg4_full_size_verify_rollback_reverify(gamma):
             lo = max(0, int(n_past[b]) - W + 1)
             kb, vb = pool_rows(cache, 0, tables[b], lo, int(n_past[b]) + T)
             ref = oracle_rows(qh[b * T:(b + 1) * T], kb, vb, window=W)
-            assert_close_rows(out[b * T:(b + 1) * T], ref, BF16_RTOL, f"seq {b}")
+            # the cfg4 shape at full size: half the bound at most
+            assert assert_close_rows(out[b * T:(b + 1) * T], ref, BF16_RTOL, f"seq {b}") <= 0.5
         return k_new, batch
 
     # ---- first speculative verify step
