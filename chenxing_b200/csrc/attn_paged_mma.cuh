@@ -92,8 +92,10 @@ __device__ __forceinline__ int plan_units(const MmaParams& p, int b, int* lo_out
 }
 
 __global__ void __launch_bounds__(1024) paged_plan_kernel(MmaParams p, int grid) {
-    __shared__ long long s_part[1024];
+    __shared__ long long s_warp[32];
+    __shared__ long long s_total;
     const int t = threadIdx.x, B = p.batch;
+    const int lane = t & 31, wid = t >> 5;
     const int per = (B + 1023) / 1024;
     const int b0 = t * per, b1 = min(B, b0 + per);
     long long local = 0;
@@ -107,15 +109,28 @@ __global__ void __launch_bounds__(1024) paged_plan_kernel(MmaParams p, int grid)
         local += (long long)plan_units(p, b, &lo) * p.n_groups;
         p.blk_lo[b] = lo;
     }
-    s_part[t] = local;
-    __syncthreads();
-    for (int off = 1; off < 1024; off <<= 1) {  // Hillis-Steele inclusive scan
-        long long v = t >= off ? s_part[t - off] : 0;
-        __syncthreads();
-        s_part[t] += v;
-        __syncthreads();
+    // block-wide exclusive scan of the per-thread unit counts: shuffle scans
+    // within each warp, then over the 32 warp totals (two block barriers)
+    long long inc = local;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const long long v = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += v;
     }
-    long long run = s_part[t] - local;  // exclusive prefix
+    if (lane == 31) s_warp[wid] = inc;
+    __syncthreads();
+    if (wid == 0) {
+        long long w = s_warp[lane];
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const long long v = __shfl_up_sync(0xffffffffu, w, off);
+            if (lane >= off) w += v;
+        }
+        s_warp[lane] = w - s_warp[lane];       // exclusive prefix of warp totals
+        if (lane == 31) s_total = w;
+    }
+    __syncthreads();
+    long long run = s_warp[wid] + inc - local;  // exclusive prefix of this thread
     for (int b = b0; b < b1; ++b) {
         p.seq_start[b] = (int)run;
         int lo;
@@ -123,7 +138,7 @@ __global__ void __launch_bounds__(1024) paged_plan_kernel(MmaParams p, int grid)
     }
     for (int i = t; i < B * p.n_groups; i += 1024) p.counters[i] = 0;
     if (t == 1023) {
-        long long W = s_part[1023];
+        long long W = s_total;
         if (W > (1ll << 30)) {
             raise_flag(CX_DEV_TABLE_OVERRUN);
             W = 0;
