@@ -174,12 +174,15 @@ __global__ void __launch_bounds__(kGenWarps * 32) attn_generic_kernel(GenericPar
             const int64_t key = k0 + lane;
             if (key < sk) {
                 if (PAGED) {
-                    const int64_t blk = table[key / p.block_size];
+                    // 32-bit division: contexts and block sizes are below 2^31
+                    const uint32_t kq = (uint32_t)key / (uint32_t)p.block_size;
+                    const uint32_t kr = (uint32_t)key - kq * (uint32_t)p.block_size;
+                    const int64_t blk = table[kq];
                     if (blk < 0 || blk >= p.n_blocks)
                         raise_flag(CX_DEV_BAD_BLOCK);
                     else
                         my_off = (((p.layer * p.n_blocks + blk) * p.hk + kh) * p.block_size +
-                                  key % p.block_size) * p.d;
+                                  kr) * p.d;
                 } else {
                     my_off = (b * p.hk + kh) * sk + key;   // row index (times d or dv below)
                 }

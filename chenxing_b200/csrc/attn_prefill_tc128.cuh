@@ -39,6 +39,22 @@
 namespace cx {
 
 constexpr int kT128Keys = 128;   // keys per key tile (S: N, PV: K)
+
+// Block ids outside the pool inside one 128-key tile (8 pool blocks).  The
+// producers load block 0 in place of such an id, so the softmax leaves the
+// block's keys out (probability 0; block 0's data is finite, so the PV product
+// adds exactly 0).  Lanes 0-7 of a softmax warp hold one id each, loaded a
+// tile ahead (tc_tile_id); the ballot gives bit k for block k of the tile.
+__device__ __forceinline__ int tc_tile_id(const int32_t* tab, int kb0, int ti, int nblk_seq,
+                                          int lane) {
+    const int blk = kb0 + ti * (kT128Keys / kBlockTok) + lane;
+    return (lane < kT128Keys / kBlockTok && blk < nblk_seq) ? tab[blk] : 0;
+}
+
+__device__ __forceinline__ unsigned tc_bad_mask(int id, int n_blocks, int lane) {
+    return __ballot_sync(0xffffffffu, lane < kT128Keys / kBlockTok && (id < 0 || id >= n_blocks)) &
+           0xffu;
+}
 constexpr int kT128Slots = 5;    // ring slots, one K or V tile each
 
 // Ring item q (the order the MMA thread reads them: K(0), K(1), V(0), K(2),
@@ -398,6 +414,8 @@ __global__ void __launch_bounds__(T128Cfg::THREADS, 1)
         const int win = p.window;
         const float sl2 = fabsf(p.scale_log2);
         constexpr int HK = kT128Keys / 2;                // keys per half
+        const int32_t* tab = p.tables + (int64_t)b * p.table_stride;
+        int nid = n_tiles > 0 ? tc_tile_id(tab, kb0, rot, nblk_seq, lane) : 0;
         float m = -INFINITY, l = 0.f;
         // `ok` turns false (warp-uniformly) when a bounded wait gives up; the
         // warp then skips its waits, TMEM and P work but keeps meeting the
@@ -421,9 +439,16 @@ __global__ void __launch_bounds__(T128Cfg::THREADS, 1)
             tc_fence_before();
             mbar_arrive(&s_free[u]);                   // S buffer u may be overwritten now
             const int ti = i + rot < n_tiles ? i + rot : i + rot - n_tiles;
+            // bad block ids of this tile's half (4 blocks), then the next tile's ids
+            const unsigned badh = (tc_bad_mask(nid, p.n_blocks, lane) >> (c * 4)) & 0xfu;
+            if (i + 1 < n_tiles) {
+                const int tn = i + 1 + rot < n_tiles ? i + 1 + rot : i + 1 + rot - n_tiles;
+                nid = tc_tile_id(tab, kb0, tn, nblk_seq, lane);
+            }
             const int kbase = kb0 * kBlockTok + ti * kT128Keys + c * HK;
             const bool edge = (kbase + HK - 1 > pos_lo) ||
-                              (win > 0 && kbase <= pos_hi - win) || (kbase + HK > ctx);
+                              (win > 0 && kbase <= pos_hi - win) || (kbase + HK > ctx) ||
+                              badh != 0;
             float mx[8];
 #pragma unroll
             for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
@@ -431,7 +456,8 @@ __global__ void __launch_bounds__(T128Cfg::THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < HK; ++j) {
                     const int key = kbase + j;
-                    const bool keep = key <= pos && key < ctx && (win <= 0 || key > pos - win);
+                    const bool keep = key <= pos && key < ctx && (win <= 0 || key > pos - win) &&
+                                      !((badh >> (j >> 4)) & 1u);
                     sv[j] = keep ? sv[j] : -INFINITY;
                     mx[j & 7] = fmaxf(mx[j & 7], sv[j]);
                 }

@@ -301,6 +301,8 @@ __global__ void __launch_bounds__(T256Cfg<DH>::THREADS, 1)
         const int pos_lo = pos0 + tw0, pos_hi = pos0 + max(tw1, tw0 + 1) - 1;
         const int win = p.window;
         const float sl2 = fabsf(p.scale_log2);
+        const int32_t* tab = p.tables + (int64_t)b * p.table_stride;
+        int nid = n_tiles > 0 ? tc_tile_id(tab, kb0, rot, nblk_seq, lane) : 0;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int i = 0; i < n_tiles; ++i) {
@@ -311,11 +313,19 @@ __global__ void __launch_bounds__(T256Cfg<DH>::THREADS, 1)
             }
             tc_fence_after();
             const int ti = i + rot < n_tiles ? i + rot : i + rot - n_tiles;
+            // bad block ids of this tile (8 blocks), then the next tile's ids
+            const unsigned bad8 = tc_bad_mask(nid, p.n_blocks, lane);
+            if (i + 1 < n_tiles) {
+                const int tn = i + 1 + rot < n_tiles ? i + 1 + rot : i + 1 + rot - n_tiles;
+                nid = tc_tile_id(tab, kb0, tn, nblk_seq, lane);
+            }
             const int kbase = kb0 * kBlockTok + ti * kT128Keys;
             const bool edge = (kbase + kT128Keys - 1 > pos_lo) ||
-                              (win > 0 && kbase <= pos_hi - win) || (kbase + kT128Keys > ctx);
+                              (win > 0 && kbase <= pos_hi - win) || (kbase + kT128Keys > ctx) ||
+                              bad8 != 0;
             auto keep = [&](int key) {
-                return key <= pos && key < ctx && (win <= 0 || key > pos - win);
+                return key <= pos && key < ctx && (win <= 0 || key > pos - win) &&
+                       !((bad8 >> ((key - kbase) >> 4)) & 1u);
             };
             // pass 1: row max over the 128 columns, 64 at a time
             float mx[8];

@@ -245,8 +245,18 @@ __global__ void __launch_bounds__(256) kv_append_rope_kernel(
     const int64_t cap = g.n_blocks * g.block_size;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t t = i / per_tok;
-        const int rem = (int)(i - t * per_tok);
+        // token and item within it: a 32-bit division where the item count
+        // allows (the 64-bit one is a long emulated sequence per item)
+        int64_t t;
+        int rem;
+        if (total <= 0xffffffffll) {
+            const uint32_t iu = (uint32_t)i, tu = iu / (uint32_t)per_tok;
+            t = tu;
+            rem = (int)(iu - tu * (uint32_t)per_tok);
+        } else {
+            t = i / per_tok;
+            rem = (int)(i - t * per_tok);
+        }
         const int row = rem / half, j = rem - row * half;
         const int64_t pos = positions[t];
         if (pos < 0 || pos >= rows) {
@@ -310,8 +320,18 @@ __global__ void __launch_bounds__(256) kv_append_rope_vec_kernel(
     const int64_t cap = g.n_blocks * g.block_size;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t t = i / per_tok;
-        const int rem = (int)(i - t * per_tok);
+        // token and item within it: a 32-bit division where the item count
+        // allows (the 64-bit one is a long emulated sequence per item)
+        int64_t t;
+        int rem;
+        if (total <= 0xffffffffll) {
+            const uint32_t iu = (uint32_t)i, tu = iu / (uint32_t)per_tok;
+            t = tu;
+            rem = (int)(iu - tu * (uint32_t)per_tok);
+        } else {
+            t = i / per_tok;
+            rem = (int)(i - t * per_tok);
+        }
         const int row = rem / gpr, p0 = (rem - row * gpr) * 8;
         const bool is_q = row < hq;
         const bool is_v = row >= hq + H;

@@ -606,6 +606,26 @@ def test_bad_block_id_leaves_its_keys_out(dtype, hk, d):
         assert np.abs(out[1:2] - ref1).max() <= F32_ATOL
 
 
+def test_bad_block_id_leaves_its_keys_out_tcgen05():
+    """The tcgen05 verify kernel reads block 0 in place of a bad id; its softmax
+    warps hold the tile's ids and give that block's keys probability 0, so the
+    rows equal attention over the other keys (16-token verify, 64 packed rows)."""
+    from chenxing_b200 import _lib
+    from gpu_cases import assert_close_rows, oracle_rows
+    case = PagedCase(hq=32, hk=8, d=128, ctx=[300, 200], q_lens=[16, 16], seed=9,
+                     q_scale=1 / np.sqrt(128), kv_scale=1.0)
+    batch = case.batch()
+    assert batch.kernel_kind(case.q_dev.dtype) == "tcgen05"
+    batch.block_tables[0, 1] = case.cache.n_blocks + 5     # keys 16..31 of sequence 0
+    out = case.run(batch)
+    assert _lib.device_flags(clear=True) & 2
+    keep = np.r_[0:16, 32:300]
+    ref0 = oracle_rows(case.q[0:16], case.k[keep], case.v[keep])
+    assert_close_rows(out[0:16], ref0, what="bad block, tcgen05")
+    ref1 = case.oracle()[1]
+    assert_close_rows(out[16:32], ref1, what="untouched sequence, tcgen05")
+
+
 def test_wait_timeout_returns_with_flag_and_next_call_is_clean():
     """The decode kernel's bounded pipeline waits: with a limit of a few
     nanoseconds the waits run out, the call still returns, CX_DEV_WAIT_TIMEOUT
