@@ -6,6 +6,8 @@
 // per CTA, head_dim 64 or 128) and attn_prefill_tc128.cuh (one query tile per
 // CTA, head_dim 128, when every sequence fits in one tile).
 #pragma once
+#include <type_traits>
+
 #include "cx_common.cuh"
 
 namespace cx {

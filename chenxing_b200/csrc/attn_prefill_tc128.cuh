@@ -40,20 +40,31 @@ namespace cx {
 
 constexpr int kT128Keys = 128;   // keys per key tile (S: N, PV: K)
 
-// Block ids outside the pool inside one 128-key tile (8 pool blocks).  The
-// producers load block 0 in place of such an id, so the softmax leaves the
-// block's keys out (probability 0; block 0's data is finite, so the PV product
-// adds exactly 0).  Lanes 0-7 of a softmax warp hold one id each, loaded a
-// tile ahead (tc_tile_id); the ballot gives bit k for block k of the tile.
-__device__ __forceinline__ int tc_tile_id(const int32_t* tab, int kb0, int ti, int nblk_seq,
-                                          int lane) {
-    const int blk = kb0 + ti * (kT128Keys / kBlockTok) + lane;
-    return (lane < kT128Keys / kBlockTok && blk < nblk_seq) ? tab[blk] : 0;
+// Block ids outside the pool.  The producers load block 0 in place of such an
+// id, so the softmax leaves the block's keys out (probability 0; block 0's
+// data is finite, so the PV product adds exactly 0).  Each softmax warp scans
+// the sequence's ids once before its key loop (tc_seq_has_bad); only when one
+// is bad does it look up each tile's 8 ids (tc_bad_mask: bit k for block k of
+// the tile).  The kernels instantiate their key loop with and without the
+// masking: masking code in the one shared loop changed how the whole softmax
+// was compiled (146 instead of 168 registers) and cost the prefill 14 %
+// (820 -> 705 TFLOP/s at head_dim 128), even with no bad id present.
+__device__ __forceinline__ bool tc_seq_has_bad(const int32_t* tab, int kb0, int nblk_seq,
+                                               int n_blocks, int lane) {
+    bool bad = false;
+#pragma unroll 4
+    for (int blk = kb0 + lane; blk < nblk_seq; blk += 32) {
+        const int id = tab[blk];
+        bad |= id < 0 || id >= n_blocks;
+    }
+    return __any_sync(0xffffffffu, bad);
 }
 
-__device__ __forceinline__ unsigned tc_bad_mask(int id, int n_blocks, int lane) {
-    return __ballot_sync(0xffffffffu, lane < kT128Keys / kBlockTok && (id < 0 || id >= n_blocks)) &
-           0xffu;
+__device__ __forceinline__ unsigned tc_bad_mask(const int32_t* tab, int kb0, int ti, int nblk_seq,
+                                                int n_blocks, int lane) {
+    const int blk = kb0 + ti * (kT128Keys / kBlockTok) + lane;
+    const int id = (lane < kT128Keys / kBlockTok && blk < nblk_seq) ? tab[blk] : 0;
+    return __ballot_sync(0xffffffffu, id < 0 || id >= n_blocks) & 0xffu;
 }
 constexpr int kT128Slots = 5;    // ring slots, one K or V tile each
 
@@ -415,12 +426,16 @@ __global__ void __launch_bounds__(T128Cfg::THREADS, 1)
         const float sl2 = fabsf(p.scale_log2);
         constexpr int HK = kT128Keys / 2;                // keys per half
         const int32_t* tab = p.tables + (int64_t)b * p.table_stride;
-        int nid = n_tiles > 0 ? tc_tile_id(tab, kb0, rot, nblk_seq, lane) : 0;
+        const bool any_bad = tc_seq_has_bad(tab, kb0, nblk_seq, p.n_blocks, lane);
         float m = -INFINITY, l = 0.f;
         // `ok` turns false (warp-uniformly) when a bounded wait gives up; the
         // warp then skips its waits, TMEM and P work but keeps meeting the
         // named barrier of the two halves, so the other warps never wait forever.
         bool ok = true;
+        // The key loop is instantiated twice: without bad-id masking (the
+        // normal case, code identical to a kernel that has none) and with it.
+        auto key_loop = [&](auto bad_tag) {
+        constexpr bool BAD = decltype(bad_tag)::value;
         for (int i = 0; i < n_tiles; ++i) {
             const int u = i & 1;
             if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[u], (i >> 1) & 1,
@@ -439,16 +454,14 @@ __global__ void __launch_bounds__(T128Cfg::THREADS, 1)
             tc_fence_before();
             mbar_arrive(&s_free[u]);                   // S buffer u may be overwritten now
             const int ti = i + rot < n_tiles ? i + rot : i + rot - n_tiles;
-            // bad block ids of this tile's half (4 blocks), then the next tile's ids
-            const unsigned badh = (tc_bad_mask(nid, p.n_blocks, lane) >> (c * 4)) & 0xfu;
-            if (i + 1 < n_tiles) {
-                const int tn = i + 1 + rot < n_tiles ? i + 1 + rot : i + 1 + rot - n_tiles;
-                nid = tc_tile_id(tab, kb0, tn, nblk_seq, lane);
-            }
+            // bad block ids of this tile's half (4 blocks)
+            const unsigned badh =
+                BAD ? (tc_bad_mask(tab, kb0, ti, nblk_seq, p.n_blocks, lane) >> (c * 4)) & 0xfu
+                    : 0u;
             const int kbase = kb0 * kBlockTok + ti * kT128Keys + c * HK;
             const bool edge = (kbase + HK - 1 > pos_lo) ||
                               (win > 0 && kbase <= pos_hi - win) || (kbase + HK > ctx) ||
-                              badh != 0;
+                              (BAD && badh != 0);
             float mx[8];
 #pragma unroll
             for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
@@ -457,7 +470,7 @@ __global__ void __launch_bounds__(T128Cfg::THREADS, 1)
                 for (int j = 0; j < HK; ++j) {
                     const int key = kbase + j;
                     const bool keep = key <= pos && key < ctx && (win <= 0 || key > pos - win) &&
-                                      !((badh >> (j >> 4)) & 1u);
+                                      (!BAD || !((badh >> (j >> 4)) & 1u));
                     sv[j] = keep ? sv[j] : -INFINITY;
                     mx[j & 7] = fmaxf(mx[j & 7], sv[j]);
                 }
@@ -528,6 +541,11 @@ __global__ void __launch_bounds__(T128Cfg::THREADS, 1)
             tc_fence_before();
             mbar_arrive(p_full);
         }
+        };
+        if (any_bad)
+            key_loop(std::true_type{});
+        else
+            key_loop(std::false_type{});
         // epilogue: row sum over both halves, then this half's 64 output columns
         // (the buffer the last tile did not use: its last readers passed the
         // last exchange barrier before this write)

@@ -302,9 +302,13 @@ __global__ void __launch_bounds__(T256Cfg<DH>::THREADS, 1)
         const int win = p.window;
         const float sl2 = fabsf(p.scale_log2);
         const int32_t* tab = p.tables + (int64_t)b * p.table_stride;
-        int nid = n_tiles > 0 ? tc_tile_id(tab, kb0, rot, nblk_seq, lane) : 0;
+        const bool any_bad = tc_seq_has_bad(tab, kb0, nblk_seq, p.n_blocks, lane);
         float m = -INFINITY, l = 0.f;
         bool ok = true;
+        // The key loop is instantiated twice: without bad-id masking (the
+        // normal case, code identical to a kernel that has none) and with it.
+        auto key_loop = [&](auto bad_tag) {
+        constexpr bool BAD = decltype(bad_tag)::value;
         for (int i = 0; i < n_tiles; ++i) {
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[w], i & 1, s_abort,
                                                             kWaitLimitNs))) {
@@ -313,19 +317,16 @@ __global__ void __launch_bounds__(T256Cfg<DH>::THREADS, 1)
             }
             tc_fence_after();
             const int ti = i + rot < n_tiles ? i + rot : i + rot - n_tiles;
-            // bad block ids of this tile (8 blocks), then the next tile's ids
-            const unsigned bad8 = tc_bad_mask(nid, p.n_blocks, lane);
-            if (i + 1 < n_tiles) {
-                const int tn = i + 1 + rot < n_tiles ? i + 1 + rot : i + 1 + rot - n_tiles;
-                nid = tc_tile_id(tab, kb0, tn, nblk_seq, lane);
-            }
+            // bad block ids of this tile (8 blocks)
+            const unsigned bad8 =
+                BAD ? tc_bad_mask(tab, kb0, ti, nblk_seq, p.n_blocks, lane) : 0u;
             const int kbase = kb0 * kBlockTok + ti * kT128Keys;
             const bool edge = (kbase + kT128Keys - 1 > pos_lo) ||
                               (win > 0 && kbase <= pos_hi - win) || (kbase + kT128Keys > ctx) ||
-                              bad8 != 0;
+                              (BAD && bad8 != 0);
             auto keep = [&](int key) {
                 return key <= pos && key < ctx && (win <= 0 || key > pos - win) &&
-                       !((bad8 >> ((key - kbase) >> 4)) & 1u);
+                       (!BAD || !((bad8 >> ((key - kbase) >> 4)) & 1u));
             };
             // pass 1: row max over the 128 columns, 64 at a time
             float mx[8];
@@ -407,6 +408,11 @@ __global__ void __launch_bounds__(T256Cfg<DH>::THREADS, 1)
             tc_fence_before();
             mbar_arrive(&p_full[w]);
         }
+        };
+        if (any_bad)
+            key_loop(std::true_type{});
+        else
+            key_loop(std::false_type{});
         // epilogue
         const bool row_ok = t < tw1;
         float* dst = p.out + ((int64_t)(qs + t) * p.hq + h * G + r % G) * D;
