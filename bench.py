@@ -517,6 +517,14 @@ def run_ours(args):
         dist.all_reduce(u, op=dist.ReduceOp.SUM)
     ms_max, units_all = float(t.item()), float(u.item())
     value = units_all / (ms_max / 1e3)
+    # every rank's step time and decode launch time: the max over ranks is set
+    # by the slowest GPU, and this shows which one and by how much
+    per_rank = None
+    if world > 1:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, {"rank": rank, "ms_per_step": ms / args.steps,
+                                          "avg_launch_ms": float(np.mean(dec_ms)),
+                                          "allgather_ms_per_step": ag_ms})
 
     # roofline of the dominant kernel (paged decode), per launch
     avg_dec_ms = float(np.mean(dec_ms))
@@ -564,7 +572,7 @@ def run_ours(args):
                 "config": workload_config(args, world, n_blocks, layers),
                 "hbm_gbs_step": step_gbs, "hbm_frac_step": step_gbs / peak,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "allgather_ms_per_step": ag_ms,
+                "allgather_ms_per_step": ag_ms, "per_rank": per_rank,
                 "gpu_launches": timed_launches, "clocks": clocks}
         if world == 1:
             return line

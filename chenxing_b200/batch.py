@@ -11,6 +11,7 @@ and ``n_tokens`` values; nothing here changes them.
 """
 from __future__ import annotations
 
+import itertools
 import math
 
 import numpy as np
@@ -26,17 +27,31 @@ def slot_mapping(block_tables, starts, counts, block_size: int) -> np.ndarray:
     """Physical slots for positions [starts[b], starts[b] + counts[b]) of each
     sequence, concatenated: ``table[p // bs] * bs + p % bs`` (the placement
     rule of write_layer, chenxing/engine/radix_kv.py:123-128)."""
-    out = []
-    for bt, s, c in zip(block_tables, starts, counts):
-        s, c = int(s), int(c)
+    starts = np.asarray(starts, dtype=np.int64).reshape(-1)
+    counts = np.asarray(counts, dtype=np.int64).reshape(-1)
+    bs = int(block_size)
+    # only the table entries each write range touches, gathered in one pass
+    parts, lens = [], []
+    for bt, s, c in zip(block_tables, starts.tolist(), counts.tolist()):
         if c == 0:
+            lens.append(0)
             continue
-        if len(bt) * block_size < s + c:
+        if len(bt) * bs < s + c:
             raise ValueError("block_table too short for requested write range")
-        pos = np.arange(s, s + c, dtype=np.int64)
-        tab = np.asarray(bt, dtype=np.int64)
-        out.append(tab[pos // block_size] * block_size + pos % block_size)
-    return np.concatenate(out) if out else np.zeros(0, dtype=np.int64)
+        seg = bt[s // bs:(s + c - 1) // bs + 1]
+        parts.append(seg)
+        lens.append(len(seg))
+    total = int(counts.sum())
+    if total == 0:
+        return np.zeros(0, dtype=np.int64)
+    ids = np.fromiter(itertools.chain.from_iterable(parts), dtype=np.int64, count=sum(lens))
+    seg_off = np.zeros(len(lens), dtype=np.int64)
+    np.cumsum(lens[:-1], out=seg_off[1:])
+    row_off = np.zeros(len(counts), dtype=np.int64)
+    np.cumsum(counts[:-1], out=row_off[1:])
+    pos = np.arange(total, dtype=np.int64) + np.repeat(starts - row_off, counts)
+    base = np.repeat(seg_off - starts // bs, counts)        # table index -> ids index
+    return ids[base + pos // bs] * bs + pos % bs
 
 
 class PagedBatch:
@@ -74,17 +89,19 @@ class PagedBatch:
         ctx = np.asarray(ctx_lens, dtype=np.int64).reshape(-1)
         if ctx.shape[0] != B:
             raise ValueError("ctx_lens and block_tables differ in length")
-        lens = [len(t) for t in block_tables]
-        stride = max(self.table_stride or 0, max(lens, default=0), 1)
-        if self.table_stride is not None and max(lens, default=0) > self.table_stride:
+        lens = np.fromiter(map(len, block_tables), dtype=np.int64, count=B)
+        longest = int(lens.max(initial=0))
+        stride = max(self.table_stride or 0, longest, 1)
+        if self.table_stride is not None and longest > self.table_stride:
             raise ValueError("a block table is longer than table_stride")
-        if np.any(ctx < 0) or np.any(ctx > np.asarray(lens, dtype=np.int64) * bs):
+        if np.any(ctx < 0) or np.any(ctx > lens * bs):
             raise ValueError("context length outside [0, len(block_table) * block_size]")
-        tab = np.zeros((B, stride), dtype=np.int32)
-        for i, t in enumerate(block_tables):
-            tab[i, :len(t)] = t
-        if B and (tab.min() < 0 or tab.max() >= self.cache.n_blocks):
+        ids = np.fromiter(itertools.chain.from_iterable(block_tables), dtype=np.int64,
+                          count=int(lens.sum()))
+        if ids.size and (ids.min() < 0 or ids.max() >= self.cache.n_blocks):
             raise IndexError(f"block id outside [0, {self.cache.n_blocks})")
+        tab = np.zeros((B, stride), dtype=np.int32)
+        tab[np.arange(stride) < lens[:, None]] = ids   # row-major mask order = concatenation
         self.batch = B
         self.stride = stride
         self.tables_host = [list(t) for t in block_tables]

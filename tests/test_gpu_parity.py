@@ -606,6 +606,28 @@ def test_bad_block_id_leaves_its_keys_out(dtype, hk, d):
         assert np.abs(out[1:2] - ref1).max() <= F32_ATOL
 
 
+@pytest.mark.parametrize("sq", [5, 9])
+def test_bad_block_id_leaves_its_keys_out_mma_verify(sq):
+    """Verify on the mma.sync kernel (20 / 36 packed rows: two / three row
+    tiles, the instances that scan their block ids up front and then run the
+    unit loop with the per-stage bad-id check): the bad block's keys are left
+    out of every query row of its sequence, the other sequence is untouched."""
+    from chenxing_b200 import _lib
+    from gpu_cases import assert_close_rows, oracle_rows
+    case = PagedCase(hq=32, hk=8, d=128, ctx=[300, 200], q_lens=[sq, sq], seed=13,
+                     q_scale=1 / np.sqrt(128), kv_scale=1.0)
+    batch = case.batch()
+    assert batch.kernel_kind(case.q_dev.dtype) == "mma"
+    batch.block_tables[0, 1] = case.cache.n_blocks + 7     # keys 16..31 of sequence 0
+    out = case.run(batch)
+    assert _lib.device_flags(clear=True) & 2
+    keep = np.r_[0:16, 32:300]
+    ref0 = oracle_rows(case.q[0:sq], case.k[keep], case.v[keep])
+    assert_close_rows(out[0:sq], ref0, what=f"bad block, mma verify sq {sq}")
+    assert_close_rows(out[sq:2 * sq], case.oracle()[1],
+                      what=f"untouched sequence, mma verify sq {sq}")
+
+
 def test_bad_block_id_leaves_its_keys_out_tcgen05():
     """The tcgen05 verify kernel reads block 0 in place of a bad id; its softmax
     warps hold the tile's ids and give that block's keys probability 0, so the

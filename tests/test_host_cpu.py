@@ -163,6 +163,60 @@ def test_slot_mapping_rejects_short_table():
         slot_mapping([[0]], [0], [3], 2)
 
 
+def test_slot_mapping_matches_the_placement_rule():
+    """slot = table[p // bs] * bs + p % bs for every written position
+    (radix_kv.py:123-128), over ragged tables, empty write ranges and ranges
+    that start mid-block."""
+    rng = np.random.default_rng(4)
+    for trial in range(200):
+        bs = int(rng.choice([1, 2, 16]))
+        B = int(rng.integers(0, 9))
+        tables, starts, counts = [], [], []
+        for _ in range(B):
+            n = int(rng.integers(0, 12))
+            tables.append(rng.integers(0, 1000, size=n).tolist())
+            cap = n * bs
+            s = int(rng.integers(0, cap + 1))
+            c = int(rng.integers(0, cap - s + 1)) if trial % 5 else 0
+            starts.append(s)
+            counts.append(c)
+        want = [t[p // bs] * bs + p % bs
+                for t, s, c in zip(tables, starts, counts) for p in range(s, s + c)]
+        got = slot_mapping(tables, starts, counts, bs)
+        assert got.dtype == np.int64
+        assert got.tolist() == want
+
+
+def test_free_list_keeps_the_reference_fifo_rules():
+    """The free list against the reference's dict-as-ordered-set: allocation
+    takes the oldest id, freeing appends, re-freeing a free id keeps its
+    place, deleting an arbitrary id (compaction) drops it; order, length and
+    membership agree after every operation of a random script."""
+    rng = np.random.default_rng(11)
+    n = 64
+    idx = RadixIndex(n, 16)
+    model = dict.fromkeys(range(n))
+    for _ in range(5000):
+        op = int(rng.integers(0, 4))
+        if op == 0 and model:
+            b = next(iter(model))
+            del model[b]
+            assert idx.alloc_block() == b
+        elif op == 1:
+            b = int(rng.integers(0, n))
+            model[b] = None
+            idx._free_block(b)
+        elif op == 2 and model:
+            b = int(rng.choice(list(model)))
+            del model[b]
+            del idx._free[b]
+        assert len(idx._free) == len(model) == idx.free_blocks
+        b = int(rng.integers(0, n))
+        assert (b in idx._free) == (b in model)
+    assert list(idx._free) == list(model)
+    assert idx._free.mask().tolist() == [int(b in model) for b in range(n)]
+
+
 def test_partition_by_context_is_balanced_and_complete():
     from chenxing_b200.workloads import lognormal_ctx
     ctx = lognormal_ctx(1024, seed=3)
