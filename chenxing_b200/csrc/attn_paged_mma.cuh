@@ -526,6 +526,7 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
         }
         s_flags[0] = 0;
         s_flags[1] = 0;
+        s_flags[2] = 0;   // verify: some block id of this CTA is outside the pool
         fence_mbar_init();
     }
     __syncthreads();
@@ -556,27 +557,30 @@ __global__ void __launch_bounds__(MmaCfg<D, MT, HG>::THREADS, 1)
     const size_t slot_floats = (size_t)HG * p.rows * (D + 2);
 
     // Verify (MT > 1): block ids outside the pool anywhere in this CTA's
-    // units, scanned once while the first stage is still loading.  The unit
-    // loop then exists in two instantiations: without bad-id handling (the
-    // normal case) and with it (read each stage's flag, leave its keys out).
-    // One loop reading the flag per unit measured 3-7 % slower at verify with
-    // no bad id present.  Decode (MT 1) keeps the one loop that reads the
-    // flag: it measured no slower, and two instantiations made it spill.
+    // units.  The consumer warps scan them together (warp w takes every NCW-th
+    // run of 32 ids) and combine the result at one named barrier, while the
+    // first stage is still loading.  The unit loop then exists in two
+    // instantiations: without bad-id handling (the normal case) and with it
+    // (read each stage's flag, leave its keys out).  Reading the flag per unit
+    // cost verify 3 % at gamma 4; each warp scanning every id itself cost 3-6 %.
+    // Decode (MT 1) keeps the one loop that reads the flag: it measured no
+    // slower, and two instantiations made it spill.
     bool any_bad = true;
     if constexpr (MT > 1) {
-        any_bad = false;
         SegCursor c2 = cur;
         Seg s2;
+        bool bad = false;
         while (c2.next(s2)) {
             const int32_t* bt = p.tables + (int64_t)s2.b * p.table_stride;
-#pragma unroll 1
-            for (int k = lane; k < s2.cnt; k += 32) {
+            for (int k = warp * 32 + lane; k < s2.cnt; k += C::NCW * 32) {
                 const int jj = s2.j0 + k;
                 const int bid = jj < p.table_stride ? bt[jj] : -1;
-                any_bad |= bid < 0 || bid >= p.n_blocks;
+                bad |= bid < 0 || bid >= p.n_blocks;
             }
         }
-        any_bad = __any_sync(0xffffffffu, any_bad);
+        if (__any_sync(0xffffffffu, bad) && lane == 0) s_flags[2] = 1;
+        named_bar_sync(1, NCT);
+        any_bad = *reinterpret_cast<volatile int*>(s_flags + 2) != 0;
     }
 
     int ibase = 0;
