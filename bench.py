@@ -1324,14 +1324,16 @@ def run_f32_decode(args):
 # the generic kernel: dense flash_attention and an fp16 pool (separate mode)
 # ---------------------------------------------------------------------------
 def run_dense(args):
-    """Two HBM-bound shapes only the tiled generic kernel serves, each its own
-    line: (1) the dense flash_attention drop-in (cx_attention_dense) at a
-    decode shape, 64 sequences x Hq 32 / Hkv 8 x 4096 keys, D 128, fp32 K/V and
-    Q, causal; (2) the cfg2 decode shape on an fp16 pool (64 sequences, ctx ~
-    U[1024, 8192], blocks scattered).  Algorithmic bytes = K + V read once +
-    Q + fp32 output (+ block tables)."""
+    """Dense attention and the generic kernel, each its own line: (1) the dense
+    flash_attention drop-in at a decode shape, 64 sequences x Hq 32 / Hkv 8 x
+    4096 keys, D 128, fp32 K/V and Q, causal (a decode-shaped fp32 call runs
+    the paged fp32 kernel over a pool view of K / V); (2) the same shape
+    through cx_attention_dense (the tiled generic kernel); (3) the cfg2
+    decode shape on an fp16 pool (64 sequences, ctx ~ U[1024, 8192], blocks
+    scattered; generic kernel).  Algorithmic bytes = K + V read once + Q +
+    fp32 output (+ block tables)."""
     import torch
-    from chenxing_b200 import PagedBatch, RadixPagedKVCache, _lib
+    from chenxing_b200 import CausalMask, PagedBatch, RadixPagedKVCache, _lib, flash_attention
     from chenxing_b200.workloads import cfg2_meta
 
     dev = torch.device("cuda", 0)
@@ -1362,13 +1364,13 @@ def run_dense(args):
             raise RuntimeError("device flags raised during the dense bench")
         return float(np.mean([a.elapsed_time(b) for a, b in evs])), clocks
 
-    def line(metric, alg, avg, clocks, workload):
+    def line(metric, alg, avg, clocks, workload, kernel="attn_generic_kernel"):
         gbs = alg / (avg / 1e3) / 1e9
         emit({"metric": metric, "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
               "warmup": args.warmup, "ms_per_step": avg, "higher_is_better": True,
               "scaling": "none", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-              "config": {"workload": workload, "kernel": "generic"},
-              "roofline": {"bound": "hbm", "kernel": "attn_generic_kernel", "achieved": gbs,
+              "config": {"workload": workload, "kernel": kernel},
+              "roofline": {"bound": "hbm", "kernel": kernel, "achieved": gbs,
                            "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_source": pk,
                            "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg},
               "clocks": clocks})
@@ -1378,12 +1380,17 @@ def run_dense(args):
     k = torch.randn((B, HK, SK, D), device=dev, generator=g)
     v = torch.randn((B, HK, SK, D), device=dev, generator=g)
     out = torch.empty((B, HQ, 1, D), dtype=torch.float32, device=dev)
+    alg = 2 * B * HK * SK * D * 4 + 2 * B * HQ * D * 4
+    shape = f"{B} seqs x {SK} keys, Hq {HQ} / Hkv {HK}, D {D}, fp32, causal"
+    mask = CausalMask()
+    avg, clocks = timed(lambda: flash_attention(q, k, v, mask))
+    line("dense flash_attention GB/s (drop-in, decode shape, fp32)", alg, avg, clocks, shape,
+         "paged_attn_f32_kernel")
     avg, clocks = timed(lambda: _lib.check(lib.cx_attention_dense(
         q.data_ptr(), _lib.CX_F32, k.data_ptr(), v.data_ptr(), _lib.CX_F32, B, HQ, 1, HK, SK, D,
         D, 1, 0, None, float("nan"), out.data_ptr(), sp), "cx_attention_dense"))
-    alg = 2 * B * HK * SK * D * 4 + 2 * B * HQ * D * 4
-    line("dense flash_attention GB/s (cx_attention_dense, decode shape, fp32)", alg, avg, clocks,
-         f"{B} seqs x {SK} keys, Hq {HQ} / Hkv {HK}, D {D}, fp32, causal")
+    line("dense attention GB/s (cx_attention_dense: generic kernel, decode shape, fp32)", alg,
+         avg, clocks, shape)
     del q, k, v, out
     torch.cuda.empty_cache()
 

@@ -126,6 +126,49 @@ def test_dense_attention_matches_reference_golden():
         np.testing.assert_allclose(got, out[c["name"]], rtol=0, atol=F32_ATOL, err_msg=c["name"])
 
 
+@pytest.mark.parametrize("b,hq,hk,sk,d,window,qbf16,routed", [
+    (3, 32, 8, 4096, 128, None, False, True),     # the dense decode bench shape, smaller batch
+    (2, 8, 2, 64, 64, None, False, True),
+    (2, 4, 4, 160, 128, 50, False, True),         # MHA, sliding window
+    (1, 16, 2, 48, 64, 1, False, True),           # window of one key
+    (2, 8, 8, 2000, 128, None, True, True),       # bf16 queries over fp32 K / V
+    (2, 8, 2, 70, 64, None, False, False),        # keys not a multiple of 16: generic kernel
+])
+def test_dense_decode_routes_through_the_paged_fp32_kernel(b, hq, hk, sk, d, window, qbf16,
+                                                           routed):
+    """flash_attention at a decode shape (one query token, causal) over fp32
+    K / V: with a key count that is a multiple of 16 it runs the paged fp32
+    kernel on a pool view of the dense arrays; either way the result is the
+    reference's fp32 attention within 1e-5 (naive semantics for windows)."""
+    import chenxing_b200.attention as att
+    from chenxing_b200 import CausalMask as Mask
+    calls = []
+    real = att._dense_decode
+
+    def spy(*a, **kw):
+        calls.append(1)
+        return real(*a, **kw)
+
+    rng = np.random.default_rng(b * 1000 + sk)
+    q = rng.standard_normal((b, hq, 1, d)).astype(np.float32)
+    if qbf16:
+        q = bf16_round(q)
+    k = rng.standard_normal((b, hk, sk, d)).astype(np.float32)
+    v = rng.standard_normal((b, hk, sk, d)).astype(np.float32)
+    att._dense_decode = spy
+    try:
+        qin = torch.from_numpy(q).to(torch.bfloat16).cuda() if qbf16 else q
+        got = att.flash_attention(qin, k, v, Mask(window))
+        got = got.cpu().numpy() if isinstance(got, torch.Tensor) else got
+    finally:
+        att._dense_decode = real
+    assert bool(calls) == routed
+    from oracle.attention import CausalMask as OMask, naive_attention as oracle_naive
+    ref = oracle_naive(q, k, v, OMask(window))
+    assert got.shape == (b, hq, 1, d)
+    assert np.abs(got - ref).max() <= F32_ATOL
+
+
 def test_dense_attention_torch_io_and_errors():
     from chenxing_b200 import CausalMask, flash_attention, gqa_expand
     q = torch.randn(1, 4, 3, 8, device="cuda")
