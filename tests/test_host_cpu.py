@@ -217,6 +217,43 @@ def test_free_list_keeps_the_reference_fifo_rules():
     assert idx._free.mask().tolist() == [int(b in model) for b in range(n)]
 
 
+def test_admission_router_is_replicable_balanced_and_conserving():
+    """Two copies of the router built from the same arguments make the same
+    finish and placement decisions (so ranks agree without messages); live
+    sets stay disjoint and complete; the KV-token spread across ranks stays
+    far below what independent per-rank admissions give."""
+    from chenxing_b200.sharding import AdmissionRouter
+    from chenxing_b200.workloads import lognormal_ctx
+    ctx = lognormal_ctx(256, seed=3)
+    groups = partition_by_context(ctx, 4)
+    a, b = (AdmissionRouter(ctx, groups, 0.05, seed=9) for _ in range(2))
+    stream = iter(lognormal_ctx(20000, seed=4))
+    rng = np.random.default_rng(0)
+    indep = [int(ctx[g].sum()) for g in groups]        # each rank refills on its own
+    indep_live = [list(ctx[g]) for g in groups]
+    for _ in range(60):
+        fa, fb = a.finish_step(), b.finish_step()
+        assert fa == fb
+        new = [int(next(stream)) for _ in range(sum(len(f) for f in fa))]
+        pa, pb = a.admit(new), b.admit(new)
+        assert pa == pb
+        assert [c for _, _, c in pa] == new
+        a.grow()
+        b.grow()
+        live = [set(a.live(r)) for r in range(4)]
+        assert sum(len(x) for x in live) == 256 and len(set().union(*live)) == 256
+        for r in range(4):
+            assert a.load[r] == sum(a.ctx[i] for i in live[r])
+        for r in range(4):                              # the unrouted comparison
+            k = max(1, round(0.05 * len(indep_live[r])))
+            for _ in range(k):
+                indep_live[r].pop(int(rng.integers(0, len(indep_live[r]))))
+            indep_live[r] += [int(x) for x in lognormal_ctx(k, seed=int(rng.integers(1 << 30)))]
+            indep[r] = sum(indep_live[r])
+    assert max(a.load) / np.mean(a.load) < 1.02
+    assert max(a.load) / np.mean(a.load) < max(indep) / np.mean(indep)
+
+
 def test_partition_by_context_is_balanced_and_complete():
     from chenxing_b200.workloads import lognormal_ctx
     ctx = lognormal_ctx(1024, seed=3)
