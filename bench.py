@@ -100,6 +100,8 @@ def workload_config(args, n_gpus, n_blocks, layers):
             "model": "Llama-3-8B attention shape (synthetic, no weights)",
             "global_batch": BATCH * n_gpus, "batch_per_gpu": BATCH,
             "seq_len": "ctx ~ U[1024, 8192] (+1 per step)", "layers": layers,
+            "sharding": "one global batch dealt to the GPUs by context length "
+                        "(equal counts, near-equal KV tokens)",
             "q_heads": HQ, "kv_heads": HK, "head_dim": D, "block_size": BS,
             "kv_dtype": "bf16", "q_dtype": "bf16", "out_dtype": "fp32",
             "pool_blocks_per_gpu": n_blocks,
@@ -409,8 +411,10 @@ def run_ours(args):
         n_blocks = int(args.pool_frac * free // per_block)
     else:
         n_blocks = BATCH * (-(-(8192 + steps_total) // BS)) + 64
-    wl = cfg2_meta(n_blocks=n_blocks, seed=args.seed + rank, batch=BATCH, steps=steps_total,
-                   n_layers=layers)
+    # one global batch of BATCH * world sequences, dealt to the ranks by length
+    # (equal counts, near-equal KV tokens); world 1 is the plain batch of 64
+    wl = cfg2_meta(n_blocks=n_blocks, seed=args.seed, batch=BATCH, steps=steps_total,
+                   n_layers=layers, world=world, rank=rank)
     cache = RadixPagedKVCache(n_blocks, BS, layers, HK, D, dtype="bfloat16", device=dev,
                               host_io=False)
     g = torch.Generator(device=dev)

@@ -17,8 +17,8 @@ import heapq
 
 import numpy as np
 
-__all__ = ["partition_by_context", "AdmissionRouter", "gather_rows", "gather_ragged_rows",
-           "max_over_ranks", "sum_over_ranks"]
+__all__ = ["partition_by_context", "deal_by_context", "AdmissionRouter", "gather_rows",
+           "gather_ragged_rows", "max_over_ranks", "sum_over_ranks"]
 
 
 def partition_by_context(ctx_lens, world: int) -> list[list[int]]:
@@ -35,6 +35,24 @@ def partition_by_context(ctx_lens, world: int) -> list[list[int]]:
         load, r = heapq.heappop(heap)
         groups[r].append(i)
         heapq.heappush(heap, (load + int(ctx[i]), r))
+    return [sorted(g) for g in groups]
+
+
+def deal_by_context(ctx_lens, world: int) -> list[list[int]]:
+    """Split sequence indices into ``world`` groups of equal size (the count
+    must divide evenly) with near-equal token sums: longest first (ties to
+    the lowest index), dealt round by round in snake order (ranks 0..world-1,
+    then world-1..0, ...), so within every round each rank takes one sequence
+    and the sums differ by at most the largest length gap of a round.
+    Indices inside a group stay ascending."""
+    ctx = np.asarray(ctx_lens, dtype=np.int64)
+    if world <= 0 or len(ctx) % world:
+        raise ValueError("deal_by_context needs a sequence count divisible by world")
+    order = sorted(range(len(ctx)), key=lambda i: (-int(ctx[i]), i))
+    groups: list[list[int]] = [[] for _ in range(world)]
+    for k, i in enumerate(order):
+        rnd, pos = divmod(k, world)
+        groups[pos if rnd % 2 == 0 else world - 1 - pos].append(i)
     return [sorted(g) for g in groups]
 
 

@@ -77,10 +77,19 @@ def cfg1(seed: int = 0, steps: int = 32):
 
 
 def cfg2_meta(n_blocks: int, seed: int = 0, batch: int = 64, steps: int = 1,
-              ctx_lo: int = 1024, ctx_hi: int = 8192, n_layers: int = 32):
-    """cfg2 metadata: tables scattered over an ``n_blocks`` pool by permutation."""
+              ctx_lo: int = 1024, ctx_hi: int = 8192, n_layers: int = 32,
+              world: int = 1, rank: int = 0):
+    """cfg2 metadata: tables scattered over an ``n_blocks`` pool by permutation.
+
+    With ``world`` > 1 the contexts of a global batch of ``batch * world``
+    sequences are drawn once and dealt to the ranks by length
+    (``deal_by_context``: ``batch`` sequences each, near-equal KV tokens), and
+    this returns rank ``rank``'s share; ``world`` = 1 is the plain batch."""
+    from .sharding import deal_by_context
     rng = np.random.default_rng(seed)
-    ctx = rng.integers(ctx_lo, ctx_hi + 1, size=batch).astype(np.int64)
+    ctx = rng.integers(ctx_lo, ctx_hi + 1, size=batch * world).astype(np.int64)
+    if world > 1:
+        ctx = ctx[deal_by_context(ctx, world)[rank]]
     perm = rng.permutation(n_blocks)
     tables = _tables_from_perm(ctx + steps, 16, perm)
     return DecodeWorkload(n_layers, 32, 8, 128, 16, n_blocks, ctx, tables, steps,

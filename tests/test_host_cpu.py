@@ -254,6 +254,27 @@ def test_admission_router_is_replicable_balanced_and_conserving():
     assert max(a.load) / np.mean(a.load) < max(indep) / np.mean(indep)
 
 
+def test_deal_by_context_equal_counts_balanced_sums():
+    """A global batch dealt to ranks by length: every rank gets the same
+    number of sequences, every index exactly once, and the token sums differ
+    by at most one round's largest length gap (far less than independent
+    per-rank draws differ)."""
+    from chenxing_b200.sharding import deal_by_context
+    rng = np.random.default_rng(1)
+    for world in (1, 2, 4, 8):
+        ctx = rng.integers(1024, 8193, size=64 * world)
+        groups = deal_by_context(ctx, world)
+        assert all(len(g) == 64 for g in groups)
+        assert sorted(i for g in groups for i in g) == list(range(64 * world))
+        assert all(g == sorted(g) for g in groups)
+        sums = [int(ctx[g].sum()) for g in groups]
+        assert max(sums) - min(sums) <= 8192 - 1024
+        if world == 1:
+            assert groups == [list(range(64))]
+    with pytest.raises(ValueError):
+        deal_by_context([1, 2, 3], 2)
+
+
 def test_partition_by_context_is_balanced_and_complete():
     from chenxing_b200.workloads import lognormal_ctx
     ctx = lognormal_ctx(1024, seed=3)
