@@ -43,10 +43,10 @@ def test_cfg4_full_size_verify_rollback_reverify(gamma):
     """B 128, ctx ~ U[2048, 16384], gamma + 1 queries per sequence, causal
     within the draft, window 4096, Hq 32 / Hkv 8, D 128, bf16 pool.
 
-    Round 1 appends and verifies the gamma + 1 chain at [ctx, ctx + gamma].
+    The first verify pass appends and verifies the gamma + 1 chain at [ctx, ctx + gamma].
     The reference then keeps ``a = gamma - rejected`` drafts plus the next
     token and shrinks ``n_tokens`` to ``ctx + a + 1`` without touching the
-    table (speculative.py:86-92, 176-184).  Round 2 grows the table like
+    table (speculative.py:86-92, 176-184).  The second pass grows the table like
     LLMEngine._ensure_capacity (engine.py:74-85), overwrites the stale slots
     with a new chain at [n', n' + gamma] and verifies again.
     """
@@ -116,7 +116,7 @@ def test_cfg4_full_size_verify_rollback_reverify(gamma):
     assert cache.free_blocks == meta.free_blocks
     for b in range(B):
         assert tables[b][:len(tables_before[b])] == tables_before[b]
-    # the accepted part of the round-1 chain, [ctx, n'), keeps its bytes
+    # the accepted part of the first pass's chain, [ctx, n'), keeps its bytes
     keep = {b: (int(ctx[b]), int(n_new[b])) for b in sample}
     before = {b: pool_rows(cache, 0, tables[b], *keep[b]) for b in sample}
     verify_round(n_new)
