@@ -160,9 +160,8 @@ class BatchedKVEngine:
         self._unhold(s.block_table)
         if self.free_private_blocks:
             # blocks no radix node and no other live table lists
-            for b in s.block_table:
-                if not c.tree_holds(b) and b not in self._held:
-                    c._free_block(b)
+            held = self._held
+            c._free_blocks([b for b in s.block_table if not c.tree_holds(b) and b not in held])
 
     def publish(self, seq_id: int) -> bool:
         """Insert the block-aligned committed prefix into the radix tree under
@@ -270,10 +269,9 @@ class BatchedKVEngine:
             if target > have:
                 need = -(-(target - have) // bs)
                 c.ensure_free(need)
-                for _ in range(need):
-                    b = c.alloc_block()
-                    s.block_table.append(b)
-                    self._held[b] += 1
+                new = c.alloc_blocks(need)
+                s.block_table.extend(new)
+                self._held.update(new)
         return StepPlan(seqs, n_past, ql, None, None, None, cow)
 
     def append(self, plan: StepPlan, layer: int, k, v) -> None:

@@ -84,16 +84,35 @@ class _FreeList:
                 self._n -= 1
                 return b
 
+    def pop_many(self, n: int) -> list:
+        """The ``n`` oldest free ids, in order (the caller checked ``len``)."""
+        q, flag, ticket = self._q, self._flag, self._ticket
+        out = []
+        while len(out) < n:
+            b, t = q.popleft()
+            if flag[b] and ticket[b] == t:
+                flag[b] = 0
+                out.append(b)
+        self._n -= n
+        return out
+
     def add(self, bid: int) -> None:
-        if self._flag[bid]:
-            return
-        self._flag[bid] = 1
-        self._ticket[bid] = self._next
-        self._q.append((bid, self._next))
-        self._next += 1
-        self._n += 1
-        if len(self._q) > 2 * len(self._flag) + 1024:     # drop stale entries
-            flag, ticket = self._flag, self._ticket
+        self.add_many((bid,))
+
+    def add_many(self, ids) -> None:
+        """Free ``ids`` in order: each goes to the back unless already free."""
+        flag, ticket, append = self._flag, self._ticket, self._q.append
+        nxt = self._next
+        for bid in ids:
+            if flag[bid]:
+                continue
+            flag[bid] = 1
+            ticket[bid] = nxt
+            append((bid, nxt))
+            nxt += 1
+        self._n += nxt - self._next
+        self._next = nxt
+        if len(self._q) > 2 * len(flag) + 1024:           # drop stale entries
             self._q = deque((b, t) for b, t in self._q if flag[b] and ticket[b] == t)
 
     def __delitem__(self, bid: int) -> None:
@@ -168,6 +187,17 @@ class RadixIndex:
 
     def _free_block(self, bid: int) -> None:
         self._free.add(bid)
+
+    def alloc_blocks(self, n: int) -> list:
+        """``n`` ``alloc_block`` calls in one: the same ids in the same order."""
+        if n > len(self._free):
+            raise OutOfKVCacheError(
+                f"KV cache exhausted ({self.n_blocks} blocks); scheduler must preempt")
+        return self._free.pop_many(n) if n > 0 else []
+
+    def _free_blocks(self, ids) -> None:
+        """``_free_block`` for each id, in order."""
+        self._free.add_many(ids)
 
     def _touch(self, node: _RadixNode) -> None:
         node.last_access = self._clock()
@@ -268,8 +298,7 @@ class RadixIndex:
             if victim is None:
                 return freed
             freed += len(victim.blocks)
-            for b in victim.blocks:
-                self._free_block(b)
+            self._free_blocks(victim.blocks)
             del victim.parent.children[victim.tokens[0]]
             self._disown(victim)
         return freed
@@ -334,8 +363,7 @@ class RadixIndex:
                 self._owned[b] += self._owned.pop(a)
         for d in dst:
             del self._free[d]
-        for s in sorted(src):
-            self._free.add(s)
+        self._free.add_many(sorted(src))
         return src, dst
 
     def stats(self) -> dict:

@@ -197,7 +197,7 @@ def test_free_list_keeps_the_reference_fifo_rules():
     idx = RadixIndex(n, 16)
     model = dict.fromkeys(range(n))
     for _ in range(5000):
-        op = int(rng.integers(0, 4))
+        op = int(rng.integers(0, 6))
         if op == 0 and model:
             b = next(iter(model))
             del model[b]
@@ -210,6 +210,21 @@ def test_free_list_keeps_the_reference_fifo_rules():
             b = int(rng.choice(list(model)))
             del model[b]
             del idx._free[b]
+        elif op == 3:                       # batch allocation: the same ids, same order
+            k = int(rng.integers(0, 6))
+            if k > len(model):
+                with pytest.raises(OutOfKVCacheError):
+                    idx.alloc_blocks(k)
+            else:
+                want = list(model)[:k]
+                for b in want:
+                    del model[b]
+                assert idx.alloc_blocks(k) == want
+        elif op == 4:                       # batch free, repeats and already-free ids included
+            ids = [int(x) for x in rng.integers(0, n, size=int(rng.integers(0, 6)))]
+            for b in ids:
+                model[b] = None
+            idx._free_blocks(ids)
         assert len(idx._free) == len(model) == idx.free_blocks
         b = int(rng.integers(0, n))
         assert (b in idx._free) == (b in model)
